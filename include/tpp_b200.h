@@ -1,0 +1,220 @@
+/*
+ * tpp_b200.h — C-ABI of the B200 (sm_100a) kernels behind torchpp's
+ * transformer-inference hot path.
+ *
+ * Every entry point takes plain device pointers, 64-bit sizes and strides
+ * (in ELEMENTS, not bytes), a dtype code and a cudaStream_t passed as void*.
+ * Nothing here allocates or frees device memory: outputs and workspaces are
+ * caller-allocated.  All launches go to the given stream (NULL = legacy
+ * default stream) and are asynchronous.  The return value is a tpp_status;
+ * on failure tpp_last_error() gives a human-readable message (thread-local).
+ *
+ * Reference interfaces replaced (paths relative to the torchpp project root):
+ *   rmsnormFused.rmsnormFused        csrc/dlops/rmsnorm/rmsnorm_binding.cu:20-73
+ *   layernormFused.applyLayernorm    csrc/dlops/layernorm/layernorm_binding.cu:8-47
+ *   ropeApplyFunction.rope_apply_cuda   csrc/dlops/rope/rope_binding.cu:10-72
+ *   qkropeApplyFunction.qkrope_apply_cuda csrc/dlops/qkrope/qkrope_binding.cu:14-101
+ *   linearActvationFp16.LinearGelu/LinearSilu/LinearRelu
+ *                                    csrc/activation/binding.cu:11-166
+ *   launchHgemv / launchHgemvCute    csrc/blas/hgemv/hgemv_kernels.cuh:69-85,240-262
+ *   flash_attn_func (third-party flash-attn 2.x, called at
+ *     torchpp/attention/gqa.py:128, swa.py:85-89, mha.py:84, mqa.py:87, ca.py:83)
+ *   KVCache.update                   torchpp/llmops/kvcache.py:50-108
+ */
+#ifndef TPP_B200_H
+#define TPP_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  TPP_OK = 0,
+  TPP_ERR_SHAPE = 1,        /* bad/mismatched sizes                          */
+  TPP_ERR_DTYPE = 2,        /* unsupported dtype code                        */
+  TPP_ERR_ALIGN = 3,        /* pointer or stride not suitably aligned        */
+  TPP_ERR_LAUNCH = 4,       /* CUDA launch/runtime error                     */
+  TPP_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up            */
+  TPP_ERR_UNSUPPORTED = 6,  /* valid request the library does not implement  */
+  TPP_ERR_WORKSPACE = 7     /* caller workspace too small / missing          */
+} tpp_status;
+
+typedef enum { TPP_F16 = 0, TPP_BF16 = 1, TPP_F32 = 2 } tpp_dtype;
+
+typedef enum {
+  TPP_ACT_NONE = 0,
+  TPP_ACT_SILU = 1,     /* x / (1 + exp(-x))            csrc/activation/activation.cuh:45-56 */
+  TPP_ACT_GELU = 2,     /* tanh GeLU                    csrc/activation/activation.cuh:26-43 */
+  TPP_ACT_RELU = 3,     /* max(x, 0)                    csrc/activation/activation.cuh:59-67 */
+  TPP_ACT_SWIGLU = 4    /* W holds [gate; up] (2N rows): y = silu(x.Wg^T) * (x.Wu^T)       */
+} tpp_act;
+
+/* ---- library info --------------------------------------------------------- */
+const char* tpp_last_error(void);
+const char* tpp_version(void);
+/* Number of kernel launches this library has issued in the calling process. */
+uint64_t tpp_launch_count(void);
+/* Reads and clears (synchronising `stream`) the current device's error flag,
+ * which a kernel sets when one of its bounded device-side waits runs out
+ * instead of spinning forever.  Returns 0 if no wait expired, the nonzero
+ * site code of the last expiry otherwise, or TPP_ERR_LAUNCH (negated: -4) if
+ * the flag could not be read.  No reference counterpart (the reference has
+ * no device-side waits). */
+int tpp_device_error(void* stream);
+
+/* ---- normalisation -------------------------------------------------------- */
+/* y[r,:] = x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w     (fp32 statistics)
+ * Replaces rmsnormFused.rmsnormFused (rmsnorm_binding.cu:20-68; kernel
+ * rmsnorm_fp16.cuh:43-115).  x,y: [rows, cols] with row strides; w: [cols]. */
+int tpp_rmsnorm(const void* x, int64_t x_row_stride, const void* w, void* y,
+                int64_t y_row_stride, int64_t rows, int64_t cols, float eps,
+                int dtype, void* stream);
+
+/* Fused residual add + RMSNorm (decode-step fusion):
+ *   res[r,:] += x[r,:];  y[r,:] = rmsnorm(res[r,:]) * w
+ * res is read and written in place (the residual stream).  When x is NULL the
+ * add is skipped.  No reference counterpart as one kernel: it fuses the
+ * "x = x + x_res; x = self.rms_norm2(x)" pair of examples/LLM/fastqwen3.py:111-114. */
+int tpp_add_rmsnorm(const void* x, void* res, const void* w, void* y,
+                    int64_t rows, int64_t cols, float eps, int dtype, void* stream);
+
+/* y = (x - mean) * rsqrt(var + eps) * w (+ b)    (two-pass fp32 statistics)
+ * Replaces layernormFused.applyLayernorm (layernorm_binding.cu:8-43; kernel
+ * layernorm_fp16.cuh:46-176, which has no bias; b may be NULL). */
+int tpp_layernorm(const void* x, const void* w, const void* b, void* y,
+                  int64_t rows, int64_t cols, float eps, int dtype, void* stream);
+
+/* ---- rotary position embedding -------------------------------------------- */
+/* NeoX rotate-half RoPE:  out = x*cos + rotate_half(x)*sin, rotate_half(x) =
+ * cat(-x[D/2:], x[:D/2]).  x is [B,H,S,D] addressed by strides (sb, sh, ss; D
+ * contiguous); out is contiguous [B,H,S,D].  cos/sin are [*, D] tables (row
+ * stride cs_stride) read at row (s + pos_offset).  Math in fp32.
+ * Replaces ropeApplyFunction.rope_apply_cuda (rope_binding.cu:10-67; kernel
+ * apply_rope.cuh:4-63). */
+int tpp_rope(const void* x, int64_t sb, int64_t sh, int64_t ss,
+             const void* cos, const void* sin, int64_t cs_stride, int cs_dtype,
+             void* out, int64_t B, int64_t H, int64_t S, int64_t D,
+             int64_t pos_offset, int dtype, void* stream);
+
+/* RoPE on Q [B,Hq,S,D] and K [B,Hk,S,D] (contiguous) in one launch; Hq may
+ * differ from Hk (GQA).  Replaces qkropeApplyFunction.qkrope_apply_cuda
+ * (qkrope_binding.cu:14-92, kernel qkrope.cuh:8-67, which required Hq == Hk). */
+int tpp_qkrope(const void* q, const void* k, const void* cos, const void* sin,
+               int64_t cs_stride, int cs_dtype, void* q_out, void* k_out,
+               int64_t B, int64_t Hq, int64_t Hk, int64_t S, int64_t D,
+               int64_t pos_offset, int dtype, void* stream);
+
+/* ---- linear layers --------------------------------------------------------- */
+/* y[M,N] = act(x[M,K] . w[N,K]^T + bias) + residual
+ * x row-major with row stride ldx (>= K); w row-major [N,K] (or [2N,K] for
+ * TPP_ACT_SWIGLU, gate rows first); bias [N] or NULL (for SWIGLU: [2N]);
+ * residual [M,N] (row stride ldy) or NULL and may alias y; y row stride ldy.
+ * fp32 accumulation.  Replaces linearActvationFp16.LinearGelu/LinearSilu/
+ * LinearRelu (activation/binding.cu:11-166, CUTLASS Sm80 GEMM of
+ * fused_gemm.cuh:143-170) and the nn.Linear projections of
+ * torchpp/attention/gqa.py:41-60.  M <= 64 runs the streaming decode kernel,
+ * larger M the tcgen05/TMEM GEMM. */
+int tpp_linear(const void* x, int64_t ldx, const void* w, const void* bias,
+               const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
+               int64_t K, int act, int dtype, void* stream);
+
+/* y[N] = W[N,K] . x[K]   (fp32 accumulation; y in dtype)
+ * Replaces launchHgemv / launchHgemvCute (hgemv_kernels.cuh:69-85, 240-262),
+ * which accumulated in fp16. */
+int tpp_hgemv(const void* W, const void* x, void* y, int64_t N, int64_t K,
+              int dtype, void* stream);
+
+/* ---- attention ----------------------------------------------------------- */
+/* Prefill / general flash attention (q_len >= 1), GQA by head mapping
+ * kv = h / (Hq/Hkv) (what repeat_interleave does at gqa.py:120-121).
+ *   q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D], o [B,Sq,Hq,D], each addressed by
+ *   (batch, seq, head) element strides with D contiguous.
+ * causal: bottom-right aligned (query i sits at key position i + Sk - Sq);
+ * window_left >= 0 limits keys to [p - window_left, p] (flash-attn
+ * window_size=(w-1,0) at swa.py:88 ⇒ window_left = w-1); -1 = unlimited.
+ * Replaces flash_attn_func(q,k,v,causal,window_size). D must be 64 or 128. */
+int tpp_attention_prefill(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh,
+                          const void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh,
+                          const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+                          void* o, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                          int64_t B, int64_t Sq, int64_t Sk, int64_t Hq, int64_t Hkv,
+                          int64_t D, int causal, int64_t window_left, float scale,
+                          int dtype, void* stream);
+
+/* Bytes of workspace tpp_attention_decode needs for the given shape. */
+int64_t tpp_attention_decode_workspace(int64_t B, int64_t Hq, int64_t max_seqlen,
+                                       int64_t D);
+
+/* Decode attention: one query token per sequence against the KV cache.
+ *   q [B,Hq,D] (strides q_sb, q_sh); caches [B,Hkv,Smax,D] (strides c_sb,
+ *   c_sh, c_ss); seqlens: device int32[B] (number of valid cache rows per
+ *   sequence, the query sits at position seqlens[b]-1) or NULL to use
+ *   max_seqlen for every sequence; o [B,Hq,D] (strides o_sb, o_sh).
+ *   window_left as in tpp_attention_prefill.  The key range is split across
+ *   CTAs (split-KV); partial results go to the caller's workspace
+ *   (tpp_attention_decode_workspace bytes) and a second kernel merges them.
+ * Replaces flash_attn_func at q_len = 1 (gqa.py:128 in the decode loop of
+ * torchpp/llmops/llm.py:263-282; sliding window swa.py:85-89). */
+int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
+                         const void* k_cache, const void* v_cache, int64_t c_sb,
+                         int64_t c_sh, int64_t c_ss, const int32_t* seqlens,
+                         int64_t max_seqlen, void* o, int64_t o_sb, int64_t o_sh,
+                         int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                         int64_t window_left, float scale, void* workspace,
+                         int64_t workspace_bytes, int dtype, void* stream);
+
+/* ---- KV cache / decode-step helpers --------------------------------------- */
+/* Fused per-head q/k RMSNorm + RoPE + KV-cache append for S new tokens.
+ *   qkv [B,S,(Hq+2*Hkv)*D] rows (row stride ld_qkv): q heads, then k, then v.
+ *   qn_w/kn_w: [D] RMSNorm weights or NULL (no q/k norm).
+ *   positions: device int32[B], the cache row of token 0 of each sequence
+ *   (token s goes to row positions[b]+s and uses cos/sin row positions[b]+s).
+ *   q_out [B,S,Hq,D] contiguous.  Caches [B,Hkv,Smax,D] (strides c_sb,c_sh,c_ss).
+ * Replaces the q_norm/k_norm (gqa.py:90-94), rope_apply (gqa.py:108-115) and
+ * KVCache.update (kvcache.py:83-108) sequence of GroupedQueryAttention.forward. */
+int tpp_qk_norm_rope_cache(const void* qkv, int64_t ld_qkv, const void* qn_w,
+                           const void* kn_w, float eps, const void* cos,
+                           const void* sin, int64_t cs_stride, int cs_dtype,
+                           const int32_t* positions, void* q_out, void* k_cache,
+                           void* v_cache, int64_t c_sb, int64_t c_sh, int64_t c_ss,
+                           int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D,
+                           int dtype, void* stream);
+
+/* Copy new K/V rows [B,Hkv,S,D] (strided) into the caches at row start_pos
+ * (host scalar) or at positions[b] when positions != NULL.
+ * Replaces the slice assignment of KVCache.update (kvcache.py:73-74, 101-102). */
+int tpp_kv_append(const void* k, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                  const void* v, int64_t v_sb, int64_t v_sh, int64_t v_ss,
+                  void* k_cache, void* v_cache, int64_t c_sb, int64_t c_sh, int64_t c_ss,
+                  int64_t B, int64_t Hkv, int64_t S, int64_t D, int64_t start_pos,
+                  const int32_t* positions, int dtype, void* stream);
+
+/* Greedy sampling: out[b] = argmax_v logits[b, v] (first index on ties), as
+ * torch.argmax in LLMInference.sample_greedy (torchpp/llmops/llm.py:181-186).
+ * logits row stride ld; out int64[B]. */
+int tpp_argmax(const void* logits, int64_t ld, int64_t B, int64_t V, int64_t* out,
+               int dtype, void* stream);
+
+/* Token embedding gather: out[t,:] = table[ids[t],:]  (nn.Embedding at
+ * examples/LLM/fastqwen3.py:128,178).  ids int64[T] on the device.  The ids
+ * are only visible on the device, so an id outside [0,V) cannot be reported
+ * synchronously: it produces a zero row instead of reading out of bounds. */
+int tpp_embedding(const int64_t* ids, int64_t T, const void* table, int64_t V,
+                  int64_t D, void* out, int dtype, void* stream);
+
+/* End-of-step bookkeeping for a device-resident (CUDA-graph) decode loop:
+ *   p = positions[b] + 1;  out_ids[b*ld_out + p] = next_tokens[b] (if p < out_cap);
+ *   positions[b] = p;  seqlens[b] = p + 1 (if seqlens != NULL).
+ * positions[b] is the cache row of the token being decoded, so after the step
+ * it points at the row of the token just produced.  Replaces the host-side
+ * torch.cat bookkeeping and per-token .item() of torchpp/llmops/llm.py:263-285. */
+int tpp_decode_advance(const int64_t* next_tokens, int64_t* out_ids, int64_t ld_out,
+                       int64_t out_cap, int32_t* positions, int32_t* seqlens, int64_t B,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPP_B200_H */

@@ -1,0 +1,108 @@
+"""Pins the CPU oracle (oracle/ops.py) against the reference's own known
+answers and golden vectors (tests/golden/golden_ref.pt, generated from the
+reference's Python by tests/golden/make_golden.py)."""
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+from oracle import ops as O
+
+G = torch.load(Path(__file__).resolve().parent / "golden" / "golden_ref.pt")
+
+
+def test_rope_tables_match_reference_compute_rope_params():
+    cos, sin = O.compute_rope_params(128, 1e6, 64)
+    assert torch.equal(cos, G["rope_cos"]) and torch.equal(sin, G["rope_sin"])
+
+
+def test_rmsnorm_matches_nn_rmsnorm_known_answer():
+    # tests/rmsnorm_test.py: nn.RMSNorm(512, eps=1e-6) is the ground truth
+    y = O.rmsnorm(G["norm_x"], G["norm_w"], 1e-6)
+    torch.testing.assert_close(y, G["rmsnorm_y"], atol=1e-5, rtol=1e-5)
+
+
+def test_layernorm_matches_nn_layernorm_known_answer():
+    # tests/layernorm_test.py: nn.LayerNorm with bias zeroed is the ground truth
+    y = O.layernorm(G["norm_x"], G["norm_w"], None, 1e-6)
+    torch.testing.assert_close(y, G["layernorm_y"], atol=1e-5, rtol=1e-5)
+
+
+def test_rope_is_rotate_half_form():
+    x = torch.randn(1, 2, 5, 8)
+    cos, sin = O.compute_rope_params(8, 1e4, 5, dtype=torch.float32)
+    y = O.rope(x, cos, sin)
+    # position 0 is the identity
+    torch.testing.assert_close(y[:, :, 0], x[:, :, 0])
+    # rotation preserves the norm of each (i, i + D/2) pair
+    n0 = x[..., :4] ** 2 + x[..., 4:] ** 2
+    n1 = y[..., :4] ** 2 + y[..., 4:] ** 2
+    torch.testing.assert_close(n0, n1, atol=1e-5, rtol=1e-5)
+
+
+def test_attention_oracle_matches_sdpa():
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(2, 7, 4, 16, generator=g)
+    k = torch.randn(2, 7, 2, 16, generator=g)
+    v = torch.randn(2, 7, 2, 16, generator=g)
+    ref = F.scaled_dot_product_attention(
+        q.transpose(1, 2), k.repeat_interleave(2, 2).transpose(1, 2),
+        v.repeat_interleave(2, 2).transpose(1, 2), is_causal=True).transpose(1, 2)
+    torch.testing.assert_close(O.attention(q, k, v, causal=True), ref, atol=1e-5, rtol=1e-5)
+
+
+def test_attention_window_and_bottom_right_alignment():
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 2, 1, 8, generator=g)
+    k = torch.randn(1, 6, 1, 8, generator=g)
+    v = torch.randn(1, 6, 1, 8, generator=g)
+    # query rows sit at absolute positions 4 and 5; window 2 => keys [p-1, p]
+    y = O.attention(q, k, v, causal=True, window_left=1)
+    for i, p in enumerate((4, 5)):
+        s = (q[0, i, 0] @ k[0, p - 1:p + 1, 0].T) / 8 ** 0.5
+        ref = torch.softmax(s, -1) @ v[0, p - 1:p + 1, 0]
+        torch.testing.assert_close(y[0, i, 0], ref, atol=1e-5, rtol=1e-5)
+
+
+def test_linear_activations():
+    g = torch.Generator().manual_seed(2)
+    x, w = torch.randn(3, 8, generator=g), torch.randn(4, 8, generator=g)
+    torch.testing.assert_close(O.linear(x, w, kind="silu"), F.silu(x @ w.T))
+    torch.testing.assert_close(O.linear(x, w, kind="gelu"),
+                               0.5 * (x @ w.T) * (1 + torch.tanh(0.7978845608028654 * (
+                                   (x @ w.T) + 0.044715 * (x @ w.T) ** 3))), atol=1e-6, rtol=1e-6)
+    w2 = torch.randn(8, 8, generator=g)
+    torch.testing.assert_close(O.linear(x, w2, kind="swiglu"),
+                               F.silu(x @ w2[:4].T) * (x @ w2[4:].T))
+
+
+def test_hgemv_known_answer_recipe():
+    # csrc/blas/hgemv/hgemv_bench.cpp:69-73 fills A[i] = i + 1, x[i] = i + 1
+    M, K = 4, 8
+    A = torch.arange(1, M * K + 1, dtype=torch.float32).view(M, K)
+    x = torch.arange(1, K + 1, dtype=torch.float32)
+    exp = torch.tensor([sum((r * K + j + 1) * (j + 1) for j in range(K)) for r in range(M)],
+                       dtype=torch.float32)
+    torch.testing.assert_close(O.hgemv(A, x), exp)
+
+
+def test_kvcache_golden_matches_reference_index_path():
+    k = torch.cat([G["kv_k0"], G["kv_k1"]], dim=2)
+    v = torch.cat([G["kv_v0"], G["kv_v1"]], dim=2)
+    torch.testing.assert_close(G["kv_k"], k)
+    torch.testing.assert_close(G["kv_v"], v)
+
+
+def test_gqa_golden_is_consistent_with_oracle_composition():
+    sd = {k[len("gqa_sd."):]: v for k, v in G.items() if k.startswith("gqa_sd.")}
+    x = G["gqa_x"]
+    B, S, _ = x.shape
+    q = (x @ sd["Wq.weight"].T).view(B, S, 4, 16)
+    k = (x @ sd["Wk.weight"].T).view(B, S, 2, 16)
+    v = (x @ sd["Wv.weight"].T).view(B, S, 2, 16)
+    pos = torch.arange(S)[None, :, None]
+    q = O.qk_norm_rope(q, sd["q_norm.weight"], 1e-6, G["gqa_cos"], G["gqa_sin"], pos)
+    k = O.qk_norm_rope(k, sd["k_norm.weight"], 1e-6, G["gqa_cos"], G["gqa_sin"], pos)
+    o = O.attention(q, k, v, causal=True).reshape(B, S, 64)
+    y = o @ sd["out_projection.weight"].T
+    torch.testing.assert_close(y, G["gqa_y"], atol=2e-3, rtol=2e-3)

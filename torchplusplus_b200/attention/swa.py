@@ -1,0 +1,53 @@
+"""SlidingWindowAttention (torchpp/attention/swa.py:8-93): causal attention
+restricted to the last `window_size` keys (flash-attn window (w-1, 0)).
+
+Deviations from the reference, which cannot run as written: it never calls
+nn.Module.__init__ (swa.py:10-11) and its q/k RMSNorm is sized embed_dim but
+applied per head (swa.py:44-46, 62-65).  Here the norms are per head
+(head_dim), like GroupedQueryAttention, and forward also accepts a KV cache
+so the window applies at decode (one query token against the cache)."""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from ._core import FusedQKV, attention_block, norm_eps
+
+
+class SlidingWindowAttention(nn.Module):
+
+    def __init__(self, window_size: int, embed_dim: int, n_heads: int, qknorm: bool = True,
+                 dtype: torch.dtype = torch.float16, n_kv_heads: int | None = None):
+        super().__init__()
+        assert embed_dim % n_heads == 0, "embed dimension should be divisible by number of heads"
+        self.window_size = window_size
+        self.embed_dim = embed_dim
+        self.n_heads = n_heads
+        self.n_kv_heads = n_kv_heads or n_heads
+        self.head_dim = embed_dim // n_heads
+        self.qknorm = qknorm
+        self.dtype = dtype
+        kv_dim = self.n_kv_heads * self.head_dim
+        self.Wq = nn.Linear(embed_dim, embed_dim, bias=False, dtype=dtype)
+        self.Wk = nn.Linear(embed_dim, kv_dim, bias=False, dtype=dtype)
+        self.Wv = nn.Linear(embed_dim, kv_dim, bias=False, dtype=dtype)
+        self.out_projection = nn.Linear(embed_dim, embed_dim, dtype=dtype)
+        if qknorm:
+            self.q_norm = nn.RMSNorm(self.head_dim, eps=1e-6, dtype=dtype)
+            self.k_norm = nn.RMSNorm(self.head_dim, eps=1e-6, dtype=dtype)
+        else:
+            self.q_norm = self.k_norm = None
+        self._qkv = FusedQKV()
+
+    def forward(self, x: torch.Tensor, cos, sin, kv_cache=None, cache_pos: Optional[int] = None):
+        w = self._qkv.get(self.Wq.weight, self.Wk.weight, self.Wv.weight)
+        return attention_block(
+            x, w, self.out_projection.weight, self.out_projection.bias, self.n_heads,
+            self.n_kv_heads, self.head_dim,
+            self.q_norm.weight if self.q_norm is not None else None,
+            self.k_norm.weight if self.k_norm is not None else None,
+            norm_eps(self.q_norm) if self.q_norm is not None else 1e-6, cos, sin,
+            kv_cache=kv_cache, cache_pos=cache_pos, causal=True,
+            window_left=self.window_size - 1)

@@ -1,0 +1,133 @@
+// Shared device/host helpers for the sm_100a kernels of libtpp_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string>
+#include "../../include/tpp_b200.h"
+
+namespace tpp {
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing: thread-local message + status codes.
+// ---------------------------------------------------------------------------
+void set_error(const std::string& msg);
+void count_launch(uint64_t n = 1);
+
+#define TPP_REQUIRE(cond, code, msg)                 \
+  do {                                               \
+    if (!(cond)) {                                   \
+      ::tpp::set_error(std::string(__func__) + ": " + (msg)); \
+      return (code);                                 \
+    }                                                \
+  } while (0)
+
+// Checks the launch that was just issued; returns TPP_ERR_LAUNCH on failure.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// ---------------------------------------------------------------------------
+// Element types.
+// ---------------------------------------------------------------------------
+template <typename T> struct Vec;  // 16-byte vector of 8 elements
+template <> struct Vec<__half> { using type = uint4; };
+template <> struct Vec<__nv_bfloat16> { using type = uint4; };
+
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+// Unpack 8 packed 16-bit elements (a uint4) into fp32.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = to_f32(e[i]);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(f[i]);
+  return u;
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+// 256-bit streaming load of data read exactly once (weights): evict-first in
+// L2, no L1 allocation.  p must be 32-byte aligned.
+__device__ __forceinline__ void ldg_stream_v8(const void* p, uint4& lo, uint4& hi) {
+  asm volatile(
+      "ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z),
+        "=r"(hi.w)
+      : "l"(p));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Activations, fp32 in/out, following csrc/activation/activation.cuh:26-67
+// of the reference (GeLU-tanh with sqrt(2/pi) and 0.044715; SiLU x/(1+e^-x)).
+__device__ __forceinline__ float act_silu(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float act_gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+__device__ __forceinline__ float act_relu(float x) { return fmaxf(x, 0.0f); }
+__device__ __forceinline__ float apply_act(int act, float x) {
+  switch (act) {
+    case TPP_ACT_SILU: return act_silu(x);
+    case TPP_ACT_GELU: return act_gelu_tanh(x);
+    case TPP_ACT_RELU: return act_relu(x);
+    default: return x;
+  }
+}
+
+// Dispatch a dtype code to a template functor.
+#define TPP_DISPATCH_HALF(dtype, T, ...)                         \
+  [&]() -> int {                                                 \
+    if ((dtype) == TPP_F16) { using T = __half; return __VA_ARGS__(); }          \
+    if ((dtype) == TPP_BF16) { using T = __nv_bfloat16; return __VA_ARGS__(); }  \
+    ::tpp::set_error(std::string(__func__) + ": dtype must be f16 (0) or bf16 (1)"); \
+    return (int)TPP_ERR_DTYPE;                                   \
+  }()
+
+}  // namespace tpp

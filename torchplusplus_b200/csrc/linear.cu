@@ -1,0 +1,40 @@
+// C-ABI entry points for linear layers: shape checks and the dispatch between
+// the decode-shaped streaming kernel (M <= 64, linear_decode.cu) and the
+// tcgen05 tensor-core GEMM (linear_tc.cu).
+#include "common.cuh"
+
+namespace tpp {
+int linear_decode(const void* x, int64_t ldx, const void* w, const void* bias,
+                  const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                  int act, int dtype, cudaStream_t st);
+int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const void* residual,
+              void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, int dtype,
+              cudaStream_t st);
+constexpr int64_t kDecodeMaxM = 64;
+}  // namespace tpp
+
+using namespace tpp;
+
+extern "C" int tpp_linear(const void* x, int64_t ldx, const void* w, const void* bias,
+                          const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
+                          int64_t K, int act, int dtype, void* stream) {
+  if (M == 0) return TPP_OK;
+  TPP_REQUIRE(x && w && y, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(M >= 0 && N > 0 && K > 0, TPP_ERR_SHAPE, "need M >= 0, N > 0, K > 0");
+  TPP_REQUIRE(M <= 0x7fffffff && N <= 0x3fffffff && K <= 0x7fffffff, TPP_ERR_SHAPE,
+              "sizes exceed 32-bit kernel indexing");
+  TPP_REQUIRE(ldx >= K && ldy >= N, TPP_ERR_SHAPE, "row stride smaller than the row");
+  TPP_REQUIRE(act >= TPP_ACT_NONE && act <= TPP_ACT_SWIGLU, TPP_ERR_UNSUPPORTED, "unknown activation");
+  TPP_REQUIRE(K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(w), TPP_ERR_ALIGN,
+              "x and W rows must be 16-byte aligned (K and ldx multiples of 8)");
+  if (M == 0) return TPP_OK;
+  cudaStream_t st = as_stream(stream);
+  if (M <= kDecodeMaxM)
+    return linear_decode(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st);
+  return linear_tc(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st);
+}
+
+extern "C" int tpp_hgemv(const void* W, const void* x, void* y, int64_t N, int64_t K, int dtype,
+                         void* stream) {
+  return tpp_linear(x, K, W, nullptr, nullptr, y, N, 1, N, K, TPP_ACT_NONE, dtype, stream);
+}

@@ -1,0 +1,27 @@
+// Library-level plumbing of the C-ABI: error messages, version, launch count.
+#include <atomic>
+#include "common.cuh"
+
+namespace tpp {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return TPP_ERR_LAUNCH;
+  }
+  count_launch();
+  return TPP_OK;
+}
+
+}  // namespace tpp
+
+extern "C" const char* tpp_last_error(void) { return tpp::g_last_error.c_str(); }
+extern "C" const char* tpp_version(void) { return "tpp_b200 0.1 (sm_100a)"; }
+extern "C" uint64_t tpp_launch_count(void) { return tpp::g_launches.load(); }
