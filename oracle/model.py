@@ -1,0 +1,91 @@
+"""fp32 CPU forward of the Qwen3-shaped decoder (test oracle only).
+
+Restates examples/LLM/fastqwen3.py:81-189 of the reference with the SwiGLU
+FFN of examples/TTS/dia/model.py:104-116: embedding -> per layer
+[x += o_proj(attn(q/k-norm, RoPE, causal GQA)(rmsnorm1(x)));
+ x += down(silu(gate(h)) * up(h)), h = rmsnorm2(x)] -> rmsnorm -> LM head.
+Parameters are read from a state dict with the names the torchpp modules use.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops as O
+
+
+@torch.no_grad()
+def forward(sd: dict, cfg, ids: torch.Tensor) -> torch.Tensor:
+    """ids [B, S] -> logits [B, S, V] (fp32), full causal attention, no cache."""
+    f = {k: v.detach().float().cpu() for k, v in sd.items()}
+    B, S = ids.shape
+    Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    cos, sin = O.compute_rope_params(D, cfg.rope_base, S)
+    pos = torch.arange(S)[None, :, None]
+    x = f["tok_embed.weight"][ids.cpu()]
+    for i in range(cfg.n_layers):
+        p = f"transformer_blocs.{i}."
+        h = O.rmsnorm(x, f[p + "rms_norm1.weight"], 1e-6)
+        q = (h @ f[p + "attn.Wq.weight"].T).view(B, S, Hq, D)
+        k = (h @ f[p + "attn.Wk.weight"].T).view(B, S, Hkv, D)
+        v = (h @ f[p + "attn.Wv.weight"].T).view(B, S, Hkv, D)
+        q = O.qk_norm_rope(q, f.get(p + "attn.q_norm.weight"), 1e-6, cos, sin, pos)
+        k = O.qk_norm_rope(k, f.get(p + "attn.k_norm.weight"), 1e-6, cos, sin, pos)
+        o = O.attention(q, k, v, causal=True).reshape(B, S, Hq * D)
+        x = x + o @ f[p + "attn.out_projection.weight"].T
+        h = O.rmsnorm(x, f[p + "rms_norm2.weight"], 1e-6)
+        g = h @ f[p + "ffn.fused_linear_layer1.weight"].T
+        u = h @ f[p + "ffn.linear_layerP.weight"].T
+        x = x + (torch.nn.functional.silu(g) * u) @ f[p + "ffn.linear_layer2.weight"].T
+    x = O.rmsnorm(x, f["final_rmsnorm.weight"], 1e-6)
+    return x @ f["out_head.weight"].T
+
+
+@torch.no_grad()
+def decode_step_cached(f: dict, cfg, tok: torch.Tensor, kc: list, vc: list, pos: int) -> torch.Tensor:
+    """One greedy decode step with a KV cache (fp32 CPU): tok [B] at position
+    `pos`; kc/vc per layer [B, Hkv, cap, D] are written at row pos.  Returns
+    the next tokens [B].  Same arithmetic as forward() restricted to one row."""
+    B = tok.shape[0]
+    Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    cos, sin = O.compute_rope_params(D, cfg.rope_base, pos + 1)
+    p_idx = torch.full((1, 1, 1), pos)
+    x = f["tok_embed.weight"][tok][:, None]                       # [B,1,E]
+    for i in range(cfg.n_layers):
+        p = f"transformer_blocs.{i}."
+        h = O.rmsnorm(x, f[p + "rms_norm1.weight"], 1e-6)
+        q = (h @ f[p + "attn.Wq.weight"].T).view(B, 1, Hq, D)
+        k = (h @ f[p + "attn.Wk.weight"].T).view(B, 1, Hkv, D)
+        v = (h @ f[p + "attn.Wv.weight"].T).view(B, 1, Hkv, D)
+        q = O.qk_norm_rope(q, f.get(p + "attn.q_norm.weight"), 1e-6, cos, sin, p_idx)
+        k = O.qk_norm_rope(k, f.get(p + "attn.k_norm.weight"), 1e-6, cos, sin, p_idx)
+        kc[i][:, :, pos] = k[:, 0]
+        vc[i][:, :, pos] = v[:, 0]
+        K = kc[i][:, :, :pos + 1].repeat_interleave(Hq // Hkv, dim=1)   # [B,Hq,L,D]
+        V = vc[i][:, :, :pos + 1].repeat_interleave(Hq // Hkv, dim=1)
+        s = torch.einsum("bhd,bhld->bhl", q[:, 0], K) / D ** 0.5
+        o = torch.einsum("bhl,bhld->bhd", torch.softmax(s, -1), V).reshape(B, 1, Hq * D)
+        x = x + o @ f[p + "attn.out_projection.weight"].T
+        h = O.rmsnorm(x, f[p + "rms_norm2.weight"], 1e-6)
+        g = h @ f[p + "ffn.fused_linear_layer1.weight"].T
+        u = h @ f[p + "ffn.linear_layerP.weight"].T
+        x = x + (torch.nn.functional.silu(g) * u) @ f[p + "ffn.linear_layer2.weight"].T
+    x = O.rmsnorm(x, f["final_rmsnorm.weight"], 1e-6)
+    return (x[:, 0] @ f["out_head.weight"].T).argmax(-1)
+
+
+def random_state_dict(cfg, std: float = 0.02, seed: int = 0) -> dict:
+    """fp32 CPU weights of the Qwen3 shape: matrices ~ N(0, std), norms 1."""
+    g = torch.Generator().manual_seed(seed)
+    E, Hq, Hkv, D, F = cfg.embed_dim, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden_dim
+    r = lambda *s: torch.randn(*s, generator=g) * std  # noqa: E731
+    sd = {"tok_embed.weight": r(cfg.vocab_size, E), "final_rmsnorm.weight": torch.ones(E),
+          "out_head.weight": r(cfg.vocab_size, E)}
+    for i in range(cfg.n_layers):
+        p = f"transformer_blocs.{i}."
+        sd.update({p + "rms_norm1.weight": torch.ones(E), p + "rms_norm2.weight": torch.ones(E),
+                   p + "attn.Wq.weight": r(Hq * D, E), p + "attn.Wk.weight": r(Hkv * D, E),
+                   p + "attn.Wv.weight": r(Hkv * D, E), p + "attn.out_projection.weight": r(E, Hq * D),
+                   p + "attn.q_norm.weight": torch.ones(D), p + "attn.k_norm.weight": torch.ones(D),
+                   p + "ffn.fused_linear_layer1.weight": r(F, E),
+                   p + "ffn.linear_layerP.weight": r(F, E), p + "ffn.linear_layer2.weight": r(E, F)})
+    return sd

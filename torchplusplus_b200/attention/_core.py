@@ -33,7 +33,7 @@ def attention_block(x: torch.Tensor, wqkv: torch.Tensor, wo: torch.Tensor,
                     qn_w: torch.Tensor | None, kn_w: torch.Tensor | None, eps: float,
                     cos: torch.Tensor | None, sin: torch.Tensor | None, kv_cache=None,
                     cache_pos: int | None = None, causal: bool = True,
-                    window_left: int = -1) -> torch.Tensor:
+                    window_left: int = -1, residual: torch.Tensor | None = None) -> torch.Tensor:
     B, S, _ = x.shape
     qkv = ops.linear(x, wqkv)                                  # [B, S, (Hq+2Hkv) D]
     if cos is None:  # no rotary embedding: identity tables
@@ -61,7 +61,7 @@ def attention_block(x: torch.Tensor, wqkv: torch.Tensor, wo: torch.Tensor,
         q = ops.qk_norm_rope_cache(qkv, qn_w, kn_w, eps, cos, sin, positions, kbuf, vbuf, Hq, Hkv)
         o = ops.attention(q, kbuf.transpose(1, 2), vbuf.transpose(1, 2), causal=causal,
                           window_left=window_left)
-    return ops.linear(o.reshape(B, S, Hq * D), wo, bo)
+    return ops.linear(o.reshape(B, S, Hq * D), wo, bo, residual=residual)
 
 
 def norm_eps(m) -> float:

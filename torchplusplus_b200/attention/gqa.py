@@ -38,7 +38,9 @@ class GroupedQueryAttention(nn.Module):
         self._qkv = FusedQKV()
 
     def forward(self, x, cos, sin, kv_cache: Optional[KVCache] = None,
-                cache_pos: Optional[int] = None):
+                cache_pos: Optional[int] = None, residual: Optional[torch.Tensor] = None):
+        """As gqa.py:70-131.  `residual` (an extension) is added to the output
+        inside the output projection's epilogue."""
         if self.DEBUG:
             print(f"\nGQA Input x shape: {x.shape}")
         w = self._qkv.get(self.Wq.weight, self.Wk.weight, self.Wv.weight)
@@ -48,4 +50,4 @@ class GroupedQueryAttention(nn.Module):
             self.q_norm.weight if self.q_norm is not None else None,
             self.k_norm.weight if self.k_norm is not None else None,
             norm_eps(self.q_norm) if self.q_norm is not None else 1e-6, cos, sin,
-            kv_cache=kv_cache, cache_pos=cache_pos, causal=True)
+            kv_cache=kv_cache, cache_pos=cache_pos, causal=True, residual=residual)

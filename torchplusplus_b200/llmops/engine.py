@@ -1,0 +1,173 @@
+"""DecodeEngine: the whole greedy decode step of a Qwen3-shaped model as ONE
+CUDA graph of sm_100a kernels, with every buffer static and the sampled token
+fed back on the device.
+
+Per step and layer: rmsnorm -> QKV linear -> fused q/k-norm + RoPE + KV write
+-> split-KV decode attention (+ merge) -> o-proj linear with the residual add
+in its epilogue -> rmsnorm -> gate/up linear with the SwiGLU product in its
+epilogue -> down linear with the residual add in its epilogue.  Then final
+rmsnorm -> LM-head linear -> argmax -> decode_advance (token history,
+positions).  Nothing returns to the host between steps.
+
+This replaces the reference's per-token Python loop (torchpp/llmops/llm.py:
+263-282), which issues ~20 launches per layer from Python, copies the whole
+cache per step (kvcache.py:106-107) and synchronises on token.item()
+(llm.py:212).
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+from .. import _native as N
+from .. import ops
+from .kvcache import KVCache
+
+
+class DecodeEngine:
+
+    def __init__(self, model, batch_size: int, max_seq_len: int):
+        cfg = model.cfg
+        dev = model.out_head.weight.device
+        self.model = model
+        self.cfg = cfg
+        self.batch_size = B = batch_size
+        self.max_seq_len = max_seq_len
+        self.device = dev
+        dt = cfg.dtype
+        self.Hq, self.Hkv, self.D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        self.eps = 1e-6
+        self.layers = []
+        for blk in model.transformer_blocs:
+            a = blk.attn
+            self.layers.append(dict(
+                n1=blk.rms_norm1.weight.detach(), n2=blk.rms_norm2.weight.detach(),
+                wqkv=a._qkv.get(a.Wq.weight, a.Wk.weight, a.Wv.weight),
+                qn=a.q_norm.weight.detach() if a.q_norm is not None else None,
+                kn=a.k_norm.weight.detach() if a.k_norm is not None else None,
+                wo=a.out_projection.weight.detach(),
+                wgu=blk.ffn.gate_up_weight(),
+                wdown=blk.ffn.linear_layer2.weight.detach()))
+        self.nf = model.final_rmsnorm.weight.detach()
+        self.lm_head = model.out_head.weight.detach()
+        self.emb = model.tok_embed.weight.detach()
+        self.cos, self.sin = model.cos, model.sin
+        if self.cos.shape[0] < max_seq_len:
+            raise ValueError("max_seq_len exceeds the model's rotary table")
+        self.caches: List[KVCache] = [
+            KVCache(max_seq_len, self.Hkv, self.D, dt, dev, batch_size=B)
+            for _ in range(cfg.n_layers)]
+        E, W = cfg.embed_dim, (self.Hq + 2 * self.Hkv) * self.D
+
+        def z(*s, d=dt):
+            return torch.zeros(*s, dtype=d, device=dev)
+        self.tokens = z(B, d=torch.int64)
+        self.positions = z(B, d=torch.int32)
+        self.seqlens = z(B, d=torch.int32)
+        self.out_ids = z(B, max_seq_len, d=torch.int64)
+        self.x, self.h = z(B, E), z(B, E)
+        self.qkv = z(B, 1, W)
+        self.q = z(B, 1, self.Hq, self.D)
+        self.o = z(B, self.Hq, self.D)
+        self.ff = z(B, cfg.hidden_dim)
+        self.logits = z(B, cfg.vocab_size)
+        nws = ops.decode_workspace_bytes(B, self.Hq, max_seq_len, self.D)
+        self.ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.launches_per_step: int | None = None
+        self.prompt_len = 0
+
+    # ------------------------------------------------------------ one step
+    def _step(self) -> None:
+        B, Hq, Hkv, D = self.batch_size, self.Hq, self.Hkv, self.D
+        ops.embedding(self.tokens, self.emb, out=self.x)
+        for L, c in zip(self.layers, self.caches):
+            ops.rmsnorm(self.x, L["n1"], self.eps, out=self.h)
+            ops.linear(self.h, L["wqkv"], out=self.qkv.view(B, -1))
+            ops.qk_norm_rope_cache(self.qkv, L["qn"], L["kn"], self.eps, self.cos, self.sin,
+                                   self.positions, c.k_cache, c.v_cache, Hq, Hkv, q_out=self.q)
+            ops.attention_decode(self.q.view(B, Hq, D), c.k_cache, c.v_cache, self.seqlens,
+                                 self.max_seq_len, out=self.o, workspace=self.ws)
+            ops.linear(self.o.view(B, Hq * D), L["wo"], residual=self.x, out=self.x)
+            ops.rmsnorm(self.x, L["n2"], self.eps, out=self.h)
+            ops.linear(self.h, L["wgu"], act="swiglu", out=self.ff)
+            ops.linear(self.ff, L["wdown"], residual=self.x, out=self.x)
+        ops.rmsnorm(self.x, self.nf, self.eps, out=self.h)
+        ops.linear(self.h, self.lm_head, out=self.logits)
+        ops.argmax(self.logits, out=self.tokens)
+        ops.decode_advance(self.tokens, self.out_ids, self.positions, self.seqlens)
+
+    def step_eager(self) -> None:
+        """One decode step launched directly (no graph); used by tests."""
+        self._step()
+
+    def capture(self) -> None:
+        """Records one decode step into a CUDA graph (the capture does not
+        execute it)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            n0 = N.launch_count()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._step()
+            self.launches_per_step = N.launch_count() - n0
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = g
+
+    # ------------------------------------------------------------ prefill
+    @torch.inference_mode()
+    def prefill(self, input_ids: torch.Tensor) -> None:
+        """Runs the prompt through the model (tensor-core GEMMs + flash
+        attention, writing the caches) and samples the first new token."""
+        B, S = input_ids.shape
+        if B != self.batch_size or S >= self.max_seq_len:
+            raise ValueError("prompt does not fit the engine's batch / capacity")
+        ids = input_ids.to(self.device, non_blocking=True)
+        for c in self.caches:
+            c.cache_len = 0
+        x = ops.embedding(ids, self.emb)
+        for blk, c in zip(self.model.transformer_blocs, self.caches):
+            x = blk(x, self.cos, self.sin, c, 0)
+        h = ops.rmsnorm(x[:, -1], self.nf, self.eps)
+        ops.linear(h, self.lm_head, out=self.logits)
+        ops.argmax(self.logits, out=self.tokens)
+        self.out_ids[:, :S].copy_(ids)
+        self.out_ids[:, S].copy_(self.tokens)
+        self.positions.fill_(S)
+        self.seqlens.fill_(S + 1)
+        self.prompt_len = S
+
+    def decode(self, steps: int) -> None:
+        if self.graph is None:
+            self.capture()
+        for _ in range(steps):
+            self.graph.replay()
+
+    @torch.inference_mode()
+    def generate(self, input_ids: torch.Tensor, max_new_token: int,
+                 eos_token_id: Optional[int] = None,
+                 stop_token_ids: Optional[list] = None, check_every: int = 16) -> torch.Tensor:
+        B, S = input_ids.shape
+        if S + max_new_token > self.max_seq_len:
+            raise ValueError("prompt + max_new_token exceeds the engine capacity")
+        self.prefill(input_ids)
+        stops = set(stop_token_ids or [])
+        if eos_token_id is not None:
+            stops.add(eos_token_id)
+        remaining = max_new_token - 1
+        done = 0
+        while remaining > 0:
+            n = min(remaining, check_every) if stops else remaining
+            self.decode(n)
+            remaining -= n
+            done += n
+            if stops:
+                cur = self.out_ids[:, S:S + 1 + done].cpu()
+                hit = torch.zeros(B, dtype=torch.bool)
+                for t in stops:
+                    hit |= (cur == t).any(dim=1)
+                if bool(hit.all()):
+                    break
+        return self.out_ids[:, :S + 1 + done]
