@@ -121,14 +121,14 @@ def main() -> None:
     #    broken in the reference, so the module is run cache-free; the
     #    cache-free call applies rope over positions 0..S-1 and a causal mask).
     torch.manual_seed(1)
-    attn = gqa_m.GroupedQueryAttention(d_in=64, num_heads=4, n_kv_heads=2, head_dim=16,
+    attn = gqa_m.GroupedQueryAttention(d_in=128, num_heads=4, n_kv_heads=2, head_dim=64,
                                        qk_norm=True, dtype=torch.float32)
     for p in attn.parameters():
         p.data = (0.1 * torch.randn(p.shape, generator=g)).half().float()
-    attn.q_norm.weight.data = (1 + 0.1 * torch.randn(16, generator=g)).half().float()
-    attn.k_norm.weight.data = (1 + 0.1 * torch.randn(16, generator=g)).half().float()
-    xg = torch.randn(2, 6, 64, generator=g).half().float()
-    c16, s16 = rope_m.compute_rope_params(16, 1e6, 6, device="cpu")
+    attn.q_norm.weight.data = (1 + 0.1 * torch.randn(64, generator=g)).half().float()
+    attn.k_norm.weight.data = (1 + 0.1 * torch.randn(64, generator=g)).half().float()
+    xg = torch.randn(2, 6, 128, generator=g).half().float()
+    c16, s16 = rope_m.compute_rope_params(64, 1e6, 6, device="cpu")
     with torch.no_grad():
         yg = attn(xg, c16, s16)
     out["gqa_x"], out["gqa_y"] = xg, yg

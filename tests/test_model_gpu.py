@@ -33,7 +33,7 @@ def make(dtype=torch.bfloat16, seed=0):
 def test_gqa_module_matches_reference_module_golden():
     G = torch.load(GOLD)
     from torchplusplus_b200.attention.gqa import GroupedQueryAttention
-    a = GroupedQueryAttention(d_in=64, num_heads=4, n_kv_heads=2, head_dim=16, qk_norm=True,
+    a = GroupedQueryAttention(d_in=128, num_heads=4, n_kv_heads=2, head_dim=64, qk_norm=True,
                               dtype=torch.float16).to(DEV)
     a.load_state_dict({k[len("gqa_sd."):]: v.half() for k, v in G.items() if k.startswith("gqa_sd.")})
     y = a(G["gqa_x"].half().to(DEV), G["gqa_cos"].to(DEV), G["gqa_sin"].to(DEV))

@@ -97,12 +97,12 @@ def test_gqa_golden_is_consistent_with_oracle_composition():
     sd = {k[len("gqa_sd."):]: v for k, v in G.items() if k.startswith("gqa_sd.")}
     x = G["gqa_x"]
     B, S, _ = x.shape
-    q = (x @ sd["Wq.weight"].T).view(B, S, 4, 16)
-    k = (x @ sd["Wk.weight"].T).view(B, S, 2, 16)
-    v = (x @ sd["Wv.weight"].T).view(B, S, 2, 16)
+    q = (x @ sd["Wq.weight"].T).view(B, S, 4, 64)
+    k = (x @ sd["Wk.weight"].T).view(B, S, 2, 64)
+    v = (x @ sd["Wv.weight"].T).view(B, S, 2, 64)
     pos = torch.arange(S)[None, :, None]
     q = O.qk_norm_rope(q, sd["q_norm.weight"], 1e-6, G["gqa_cos"], G["gqa_sin"], pos)
     k = O.qk_norm_rope(k, sd["k_norm.weight"], 1e-6, G["gqa_cos"], G["gqa_sin"], pos)
-    o = O.attention(q, k, v, causal=True).reshape(B, S, 64)
+    o = O.attention(q, k, v, causal=True).reshape(B, S, 256)
     y = o @ sd["out_projection.weight"].T
     torch.testing.assert_close(y, G["gqa_y"], atol=2e-3, rtol=2e-3)

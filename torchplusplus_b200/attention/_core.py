@@ -12,6 +12,13 @@ import torch
 from .. import ops
 
 
+def _version(t: torch.Tensor) -> int:
+    try:
+        return t._version
+    except RuntimeError:  # inference tensors carry no version counter
+        return -1
+
+
 class FusedQKV:
     """Caches cat(Wq, Wk, Wv) so one GEMM produces q, k and v; rebuilt when any
     weight changes (tracked through the tensors' version counters)."""
@@ -21,7 +28,7 @@ class FusedQKV:
         self._w = None
 
     def get(self, *ws: torch.Tensor) -> torch.Tensor:
-        key = tuple((w.data_ptr(), w._version, w.shape) for w in ws)
+        key = tuple((w.data_ptr(), _version(w), w.shape) for w in ws)
         if key != self._key:
             self._w = torch.cat([w.detach() for w in ws], dim=0).contiguous()
             self._key = key

@@ -305,12 +305,13 @@ static int qnrc_launch(const void* qkv, int64_t ld, const void* qn, const void* 
     return check_launch("qk_norm_rope_cache_kernel");
   };
   switch (D) {
+    case 16: return go(std::integral_constant<int, 2>{});
     case 32: return go(std::integral_constant<int, 4>{});
     case 64: return go(std::integral_constant<int, 8>{});
     case 128: return go(std::integral_constant<int, 16>{});
     case 256: return go(std::integral_constant<int, 32>{});
     default:
-      set_error("tpp_qk_norm_rope_cache: head dim must be 32, 64, 128 or 256");
+      set_error("tpp_qk_norm_rope_cache: head dim must be 16, 32, 64, 128 or 256");
       return TPP_ERR_UNSUPPORTED;
   }
 }
