@@ -165,6 +165,27 @@ int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
                          int64_t window_left, float scale, void* workspace,
                          int64_t workspace_bytes, int dtype, void* stream);
 
+/* Allocation-free decode attention: the same computation and arguments as
+ * tpp_attention_decode, minus the workspace.  For callers that cannot
+ * allocate device memory when they decode (allocator / memory-pool
+ * callbacks, runtimes with a fixed memory budget that forbid cudaMalloc after
+ * start-up, plain-C hosts without an allocator to carve a workspace from).
+ * The split-KV partials go to a fixed 8 MiB scratch array inside the
+ * library's device image, held by every GPU that loads the library until
+ * exit; shapes needing more (see tpp_attention_decode_workspace) are rejected
+ * with TPP_ERR_WORKSPACE.  All calls on a device share that array, so calls
+ * that overlap on the GPU race -- serialise them.  The first call on each
+ * device looks the array's address up; make it before any stream capture.
+ * Allocates nothing.  No counterpart in the reference. */
+int tpp_attention_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
+                                 const void* k_cache, const void* v_cache, int64_t c_sb,
+                                 int64_t c_sh, int64_t c_ss, const int32_t* seqlens,
+                                 int64_t max_seqlen, void* o, int64_t o_sb, int64_t o_sh,
+                                 int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                 int64_t window_left, float scale, int dtype, void* stream);
+/* Size in bytes of that fixed scratch array.  No counterpart in the reference. */
+int64_t tpp_attention_decode_noalloc_max_bytes(void);
+
 /* ---- KV cache / decode-step helpers --------------------------------------- */
 /* Fused per-head q/k RMSNorm + RoPE + KV-cache append for S new tokens.
  *   qkv [B,S,(Hq+2*Hkv)*D] rows (row stride ld_qkv): q heads, then k, then v.

@@ -56,6 +56,10 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_attention_decode_workspace": (_i64, [_i64, _i64, _i64, _i64]),
     "tpp_attention_decode": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i64,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
+    "tpp_attention_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64,
+                                            _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32,
+                                            _i32, _p]),
+    "tpp_attention_decode_noalloc_max_bytes": (_i64, []),
     "tpp_qk_norm_rope_cache": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _i32, _p, _p, _p, _p,
                                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p]),
     "tpp_kv_append": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _i64,

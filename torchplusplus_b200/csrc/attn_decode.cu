@@ -19,6 +19,7 @@
 //    writes (o, lse) partials to the workspace and decode_combine_kernel
 //    merges the splits.
 #include <math.h>
+#include <mutex>
 #include "common.cuh"
 
 namespace tpp {
@@ -332,4 +333,81 @@ extern "C" int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
   return attn_decode_run(q, q_sb, q_sh, k_cache, v_cache, c_sb, c_sh, c_ss, seqlens, max_seqlen,
                          o, o_sb, o_sh, B, Hq, Hkv, D, window_left, scale, workspace,
                          workspace_bytes, dtype, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of tpp_attention_decode.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// code running inside a custom allocator or memory-pool callback, runtimes
+// that forbid cudaMalloc after start-up (fixed memory budgets, real-time
+// serving loops), and plain-C hosts that have no allocator of their own to
+// hand a workspace from.  This entry point keeps the split-KV partial results
+// in a fixed scratch array that lives in this library's device image instead
+// of a caller workspace.  It never calls cudaMalloc/cudaFree.
+//
+// Limits and sharing: the array holds kNoAllocScratchBytes (8 MiB) on every
+// GPU that loads the library, until the process exits.  Every call on a
+// device uses the same array, so calls whose kernels overlap on the GPU (two
+// streams at once, or two host threads) race on it; serialise them.  Nothing
+// in the array has to start at zero: each call writes every partial it later
+// reads.  The first call on each device looks up the array's device address
+// (cudaGetSymbolAddress) -- make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::mutex g_scratch_mu;
+
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("tpp_attention_decode_noalloc: no usable current CUDA device");
+    return TPP_ERR_LAUNCH;
+  }
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(std::string("tpp_attention_decode_noalloc: cudaGetSymbolAddress failed: ") +
+                cudaGetErrorString(e));
+      return TPP_ERR_LAUNCH;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return TPP_OK;
+}
+}  // namespace
+
+extern "C" int64_t tpp_attention_decode_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int tpp_attention_decode_noalloc(const void* q, int64_t q_sb, int64_t q_sh,
+                                            const void* k_cache, const void* v_cache,
+                                            int64_t c_sb, int64_t c_sh, int64_t c_ss,
+                                            const int32_t* seqlens, int64_t max_seqlen, void* o,
+                                            int64_t o_sb, int64_t o_sh, int64_t B, int64_t Hq,
+                                            int64_t Hkv, int64_t D, int64_t window_left,
+                                            float scale, int dtype, void* stream) {
+  if (B == 0) return TPP_OK;
+  TPP_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && D > 0 && max_seqlen >= 0,
+              TPP_ERR_SHAPE, "bad sizes");
+  int64_t range = max_seqlen;
+  if (window_left >= 0 && window_left + 1 < range) range = window_left + 1;
+  const int64_t need = attn_decode_workspace_bytes(B, Hq, Hkv, range, D);
+  TPP_REQUIRE(need <= kNoAllocScratchBytes, TPP_ERR_WORKSPACE,
+              "this shape needs " + std::to_string(need) + " bytes of split-KV scratch, more "
+              "than the fixed " + std::to_string(kNoAllocScratchBytes) +
+              " bytes; use tpp_attention_decode with a caller workspace");
+  void* ws = nullptr;
+  if (need > 0) {
+    const int rc = scratch_for_current_device(&ws);
+    if (rc != TPP_OK) return rc;
+  }
+  return attn_decode_run(q, q_sb, q_sh, k_cache, v_cache, c_sb, c_sh, c_ss, seqlens, max_seqlen,
+                         o, o_sb, o_sh, B, Hq, Hkv, D, window_left, scale, ws,
+                         kNoAllocScratchBytes, dtype, as_stream(stream));
 }
