@@ -308,6 +308,7 @@ def run_ours(args, rank, world, local):
 
 
 def main():
+    global GEN
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -317,7 +318,10 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-b1", action="store_true")
+    ap.add_argument("--gen", type=int, default=GEN,
+                    help="tokens generated per request (profiling runs use fewer)")
     args = ap.parse_args()
+    GEN = args.gen
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", 0))
         run_reference(args, rank, int(os.environ.get("WORLD_SIZE", 1)))

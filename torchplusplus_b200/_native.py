@@ -13,7 +13,8 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtpp_b200.so"
+LIB_PATH = Path(os.environ.get("TPP_LIB") or
+                Path(__file__).resolve().parent / "_lib" / "libtpp_b200.so")
 
 TPP_OK = 0
 STATUS_NAMES = {

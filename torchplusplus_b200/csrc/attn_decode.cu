@@ -56,6 +56,8 @@ struct DecodeArgs {
 
 template <typename T, int D, int GP>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(DecodeArgs p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int LG = D / 8;            // lanes per stream
   constexpr int NS = kThreads / LG;    // streams per CTA
   constexpr int U = 4;                 // keys per step
@@ -108,16 +110,25 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(DecodeArgs p) {
 
   // The trip count is uniform across the CTA (the shuffles below need whole
   // warps); keys past k1 are masked.
+  // Register double buffer: the rows of the next step are requested before
+  // the current step's math, so each stream always has 2*U K/V rows in flight.
+  uint4 nk[U], nv[U];
+  auto fetch = [&](int64_t it) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t key = it + stream + (int64_t)u * NS;
+      const bool ok = key < k1;
+      nk[u] = ok ? ldg_nc_v4(Kb + key * p.c_ss) : z;
+      nv[u] = ok ? ldg_nc_v4(Vb + key * p.c_ss) : z;
+    }
+  };
+  fetch(k0);
   for (int64_t it = k0; it < k1; it += (int64_t)NS * U) {
     const int64_t base = it + stream;
     uint4 kr[U], vr[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t key = base + (int64_t)u * NS;
-      const bool ok = key < k1;
-      kr[u] = ok ? ldg_nc_v4(Kb + key * p.c_ss) : z;
-      vr[u] = ok ? ldg_nc_v4(Vb + key * p.c_ss) : z;
-    }
+    for (int u = 0; u < U; ++u) { kr[u] = nk[u]; vr[u] = nv[u]; }
+    fetch(it + (int64_t)NS * U);
     float s[U][GP];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -199,6 +210,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(DecodeArgs p) {
 // One warp per (batch, q head): merges the splits' (o, lse) partials.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs p, int64_t B) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= B * p.Hq) return;
@@ -236,18 +249,18 @@ int decode_launch(DecodeArgs& a, int64_t B, cudaStream_t st) {
   const int gp = a.G >= 8 ? 8 : (a.G >= 4 ? 4 : (a.G >= 2 ? 2 : 1));
   const int passes = (a.G + gp - 1) / gp;
   dim3 grid((unsigned)a.num_splits, (unsigned)(a.Hkv * passes), (unsigned)B);
+  int rc = TPP_OK;
   switch (gp) {
-    case 1: decode_attn_kernel<T, D, 1><<<grid, kThreads, 0, st>>>(a); break;
-    case 2: decode_attn_kernel<T, D, 2><<<grid, kThreads, 0, st>>>(a); break;
-    case 4: decode_attn_kernel<T, D, 4><<<grid, kThreads, 0, st>>>(a); break;
-    default: decode_attn_kernel<T, D, 8><<<grid, kThreads, 0, st>>>(a); break;
+    case 1: rc = launch("decode_attn_kernel", decode_attn_kernel<T, D, 1>, dim3(grid), dim3(kThreads), 0, st, 0, a); break;
+    case 2: rc = launch("decode_attn_kernel", decode_attn_kernel<T, D, 2>, dim3(grid), dim3(kThreads), 0, st, 0, a); break;
+    case 4: rc = launch("decode_attn_kernel", decode_attn_kernel<T, D, 4>, dim3(grid), dim3(kThreads), 0, st, 0, a); break;
+    default: rc = launch("decode_attn_kernel", decode_attn_kernel<T, D, 8>, dim3(grid), dim3(kThreads), 0, st, 0, a); break;
   }
-  int rc = check_launch("decode_attn_kernel");
   if (rc != TPP_OK || a.num_splits == 1) return rc;
   const int64_t warps = B * a.Hq;
   const int64_t blocks = (warps * 32 + 255) / 256;
-  decode_combine_kernel<T, D><<<(unsigned)blocks, 256, 0, st>>>(a, B);
-  return check_launch("decode_combine_kernel");
+  return launch("decode_combine_kernel", decode_combine_kernel<T, D>, dim3((unsigned)blocks),
+                dim3(256), 0, st, 0, a, B);
 }
 
 }  // namespace

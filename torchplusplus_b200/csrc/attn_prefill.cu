@@ -94,6 +94,8 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(PrefillArgs p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int CH = D / 8;  // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sQ = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -287,8 +289,7 @@ int prefill_launch(const PrefillArgs& a, int64_t B, cudaStream_t st) {
     return TPP_ERR_LAUNCH;
   }
   dim3 grid((unsigned)((a.Sq + BLOCK_M - 1) / BLOCK_M), (unsigned)a.Hq, (unsigned)B);
-  kern<<<grid, kThreads, smem, st>>>(a);
-  return check_launch("prefill_attn_kernel");
+  return launch("prefill_attn_kernel", kern, dim3(grid), dim3(kThreads), smem, st, 0, a);
 }
 
 }  // namespace

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 #include "../../include/tpp_b200.h"
 
 namespace tpp {
@@ -119,6 +120,55 @@ __device__ __forceinline__ float apply_act(int act, float x) {
     case TPP_ACT_RELU: return act_relu(x);
     default: return x;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  Every kernel of this library is
+// launched with programmatic stream serialization allowed, calls pdl_wait()
+// before it touches memory written by earlier work on the stream (and before
+// its first global write), and pdl_trigger() once its dependents may be
+// scheduled.  The next kernel can therefore be resident and run its
+// independent prologue (e.g. start streaming weights) while this one drains.
+// Outside a PDL launch both instructions are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// PDL on unless the environment sets TPP_PDL=0 (for A/B measurements).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           cudaStream_t st, unsigned cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return TPP_ERR_LAUNCH;
+  }
+  return check_launch(what);
 }
 
 // Dispatch a dtype code to a template functor.

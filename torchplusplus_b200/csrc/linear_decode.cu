@@ -1,277 +1,416 @@
 // Decode-shaped linear layers: y[M,N] = epilogue(x[M,K] . W[N,K]^T) for M <= 64.
 //
 // At decode the weight matrix is read exactly once per step and the token
-// count is tiny, so the kernel is bound by HBM bandwidth on W.  Design:
-//  * A warp owns 16 weight rows (the M side of an m16n8k16 tensor-core MMA;
-//    tokens are the N side, 8 per MMA tile).  W is streamed straight from HBM
-//    into registers with 16-byte evict-first loads; no shared-memory staging.
-//  * K is processed in 64-element chunks.  Lane (g, c) of the warp loads
-//    elements [16c, 16c+16) of the chunk for rows g and g+8, i.e. a whole
-//    128-byte line per row per chunk.  Those 16 physical k are assigned to the
-//    MMA's logical k slots by a fixed permutation that depends on c only, and
-//    the activation fragment (x) is loaded with the same permutation, so the
-//    dot product is unchanged (a sum over k is order independent).
-//  * K is split across the 8 warps of a CTA and, for short-and-wide matrices,
-//    across the CTAs of a thread-block cluster (up to 8).  Partial tiles are
-//    reduced in shared memory and then over distributed shared memory into
-//    the cluster's rank-0 CTA, which runs the fused epilogue (bias,
-//    activation, SwiGLU gate*up, residual add).  No global scratch.
+// count is tiny, so the kernel is bound by HBM bandwidth on W.  Design
+// ("swap-AB" on the 5th-generation tensor cores):
+//  * The MMA's M side is 128 weight rows, its N side the (padded) tokens
+//    (BN = 16/32/64): D[128 x BN] += W_tile[128 x 64] . x_tile[BN x 64]^T with
+//    tcgen05.mma kind::f16, fp32 accumulator in TMEM (BN columns).
+//  * W and x tiles arrive by TMA (128-byte swizzle, no multicast) in a
+//    kStages-deep shared-memory ring guarded by full/empty mbarriers: up to
+//    kStages x 16 KB of weights in flight per CTA, independent of registers.
+//  * The first kStages weight tiles are requested BEFORE the programmatic-
+//    dependent-launch wait: weights never depend on the previous kernel, so
+//    they stream while that kernel drains.  x tiles follow after the wait.
+//  * Short-and-wide matrices split K over the CTAs of a thread-block cluster
+//    (1, 2, 4 or 8).  The tile's outputs are divided among the ranks; every
+//    rank pushes its TMEM partial rows to their owners with remote shared-
+//    memory stores, and after one cluster barrier each owner sums its slice
+//    and runs the fused epilogue (bias, activation, SwiGLU gate*up, residual
+//    add).  No global scratch.
+//  * Epilogue stores are staged through shared memory as [token][output] so
+//    y is written with coalesced 16-byte stores.
+//  * SwiGLU: the 128-row A tile holds 64 gate rows then the 64 matching up
+//    rows (two TMA boxes), so one tile yields 64 outputs silu(g)*u.
+// Roles in the 128-thread CTA: warp 0 / lane 0 issues TMA, warp 1 / lane 0
+// issues MMAs, all 4 warps run the epilogue (warp w owns TMEM lanes
+// 32w..32w+31 = tile rows).
 // Reference: the unbuilt hgemv kernels csrc/blas/hgemv/hgemv_kernels.cuh:19-85
-// (one warp per row, fp16 accumulation) and the CUTLASS fused linear of
-// csrc/activation/fused_gemm.cuh:143-170 (128x128 tiles, which waste >= 75% of
-// the MMA at M <= 32).  Accumulation here is fp32.
+// (one warp per row, fp16 accumulation) and the CUTLASS Sm80 fused linear of
+// csrc/activation/fused_gemm.cuh:143-170 (128x128 tiles over M, which waste
+// >= 75% of the MMA at M <= 32).  Accumulation here is fp32.
 #include <cooperative_groups.h>
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace tpp {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int BM = 128;  // weight rows per tile (MMA M)
+constexpr int BK = 64;   // 128 bytes: one swizzle row
+constexpr int kStages = 5;
+constexpr int kThreads = 128;
+constexpr uint32_t kStageA = BM * BK * 2;  // 16 KB
 
-template <typename T>
-__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1);
-template <>
-__device__ __forceinline__ void mma16816<__half>(float* d, const uint32_t* a, uint32_t b0,
-                                                 uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-__device__ __forceinline__ void mma16816<__nv_bfloat16>(float* d, const uint32_t* a, uint32_t b0,
-                                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+template <int BN>
+constexpr uint32_t stage_b() { return BN * BK * 2; }
+template <int BN>
+constexpr size_t smem_bytes() {
+  return (size_t)kStages * (kStageA + stage_b<BN>()) + 1024 + 256;
 }
 
-__device__ __forceinline__ uint32_t pick(const uint4& lo, const uint4& hi, int i) {
-  switch (i) {
-    case 0: return lo.x; case 1: return lo.y; case 2: return lo.z; case 3: return lo.w;
-    case 4: return hi.x; case 5: return hi.y; case 6: return hi.z; default: return hi.w;
+struct SkinnyArgs {
+  const void* bias;
+  const void* residual;
+  void* y;
+  int64_t ldy;
+  int M, N, K;
+  int act;
+  int kb_per_split;
+  int vec_ok;
+  int* err;
+};
+
+#ifdef TPP_DEBUG_STAMPS
+__device__ unsigned long long g_dbg_stamps[8 * 4096];
+#endif
+
+template <int BN>
+__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  if constexpr (BN == 16) {
+    tmem_ld16(taddr, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  } else {
+#pragma unroll
+    for (int h = 0; h < BN / 32; ++h) {
+      tmem_ld32(taddr + h * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[h * 32 + j] = __uint_as_float(r[j]);
+    }
   }
 }
 
-struct LinearArgs {
-  const void* x; int64_t ldx;
-  const void* w;
-  const void* bias;
-  const void* residual;
-  void* y; int64_t ldy;
-  int M, N, K;
-  int act;
-  int chunks_per_split;  // 64-element K chunks per (warp, cluster-rank) split
-};
+template <typename T, int BN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_skinny_kernel(const __grid_constant__ CUtensorMap tm_w,
+                         const __grid_constant__ CUtensorMap tm_x, SkinnyArgs p) {
+  constexpr uint32_t kStageB = stage_b<BN>();
+  constexpr int TCOLS = BN < 32 ? 32 : BN;  // TMEM allocation (power of 2 >= 32)
+  constexpr int NOUT = SWIGLU ? BM / 2 : BM;
+  constexpr int RS = BN + 1;   // padded row stride for the SwiGLU hand-over (odd: no conflicts)
+  constexpr int RSV = BN + 4;  // row stride of the split-K receive buffer (16-byte rows)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kStageB);
+  uint64_t* empty = full + kStages;
+  uint64_t* accum = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  // Reused once every MMA has completed: the split-K receive buffer (128 rows
+  // in total over all source ranks) and the rank's staged output slice.
+  float* recv = reinterpret_cast<float*>(smem);            // [csize][rows][RS]
+  float* stage = recv + BM * RSV;                           // [BN][NOUT/csize + 1]
 
-// NRG: row sets per CTA (1, or 2 for SwiGLU gate+up). MT: 8-token MMA tiles.
-template <typename T, int NRG, int MT, bool V8>
-__global__ void __launch_bounds__(kThreads) linear_decode_kernel(LinearArgs p) {
-  constexpr int WK = kWarps / NRG;  // warps along K per row set
-  constexpr int TOK = MT * 8;
-  extern __shared__ float smem[];
-  float* part = smem;                              // [kWarps][16][TOK]
-  float* red = smem + kWarps * 16 * TOK;           // [NRG][16][TOK]
-
+#ifdef TPP_DEBUG_STAMPS
+  unsigned long long stamps[8];
+  auto ts = [&](int i) { asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(stamps[i])); };
+  ts(0);
+#define TPP_TS(i) ts(i)
+#else
+#define TPP_TS(i)
+#endif
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int csize = (int)cluster.num_blocks();
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int rs = warp / WK;       // row set (0 = plain/gate, 1 = up)
-  const int wk = warp % WK;
-  const int row_base = blockIdx.x * 16 + (rs ? p.N : 0);
-  const int rows_total = NRG == 2 ? 2 * p.N : p.N;
-  const int ra = blockIdx.x * 16 + g;  // row within the set
-  const int rowA = row_base + g, rowB = row_base + g + 8;
-  const bool okA = ra < p.N, okB = ra + 8 < p.N;
-  (void)rows_total;
+  const int out0 = blockIdx.x * NOUT;  // first output feature of this tile
+  const int nkb = (p.K + BK - 1) / BK;
+  const int kb0 = crank * p.kb_per_split;
+  const int kb1 = min(nkb, kb0 + p.kb_per_split);
+  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
 
-  const T* W = static_cast<const T*>(p.w);
-  const T* X = static_cast<const T*>(p.x);
-  const int nchunks = (p.K + 63) >> 6;
-  const int split = crank * WK + wk;
-  const int c0 = split * p.chunks_per_split;
-  const int c1 = min(nchunks, c0 + p.chunks_per_split);
-
-  float acc[MT][4];
-#pragma unroll
-  for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
-
-  const T* wA = W + (int64_t)rowA * p.K;
-  const T* wB = W + (int64_t)rowB * p.K;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-
-  constexpr int U = 2;  // chunks in flight per iteration
-  for (int j0 = c0; j0 < c1; j0 += U) {
-    uint4 a[U][4];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = j0 + u;
-      const int k = j * 64 + c * 16;
-      const bool in = j < c1;
-      const bool k0 = in && k < p.K, k1 = in && k + 8 < p.K;
-      if (V8 && k1) {
-        // whole 32-byte run in range: one 256-bit load per row
-        if (okA) ldg_stream_v8(wA + k, a[u][0], a[u][1]); else { a[u][0] = z; a[u][1] = z; }
-        if (okB) ldg_stream_v8(wB + k, a[u][2], a[u][3]); else { a[u][2] = z; a[u][3] = z; }
-      } else {
-        a[u][0] = (okA && k0) ? ldg_nc_v4(wA + k) : z;
-        a[u][1] = (okA && k1) ? ldg_nc_v4(wA + k + 8) : z;
-        a[u][2] = (okB && k0) ? ldg_nc_v4(wB + k) : z;
-        a[u][3] = (okB && k1) ? ldg_nc_v4(wB + k + 8) : z;
-      }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_x);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int j = j0 + u;
-      if (j >= c1) break;
-      const int k = j * 64 + c * 16;
-      const bool k0 = k < p.K, k1 = k + 8 < p.K;
-#pragma unroll
-      for (int t = 0; t < MT; ++t) {
-        const int tok = t * 8 + g;
-        uint4 blo = z, bhi = z;
-        if (tok < p.M) {
-          const T* xr = X + (int64_t)tok * p.ldx + k;
-          if (k0) blo = __ldg(reinterpret_cast<const uint4*>(xr));
-          if (k1) bhi = __ldg(reinterpret_cast<const uint4*>(xr + 8));
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t af[4];
-          af[0] = pick(a[u][0], a[u][1], 2 * q);
-          af[1] = pick(a[u][2], a[u][3], 2 * q);
-          af[2] = pick(a[u][0], a[u][1], 2 * q + 1);
-          af[3] = pick(a[u][2], a[u][3], 2 * q + 1);
-          mma16816<T>(acc[t], af, pick(blo, bhi, 2 * q), pick(blo, bhi, 2 * q + 1));
-        }
-      }
-    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
   }
-
-  // ---- reduction: warps -> CTA -> cluster rank 0 ----
-#pragma unroll
-  for (int t = 0; t < MT; ++t) {
-    float* pw = part + warp * 16 * TOK;
-    pw[g * TOK + t * 8 + 2 * c] = acc[t][0];
-    pw[g * TOK + t * 8 + 2 * c + 1] = acc[t][1];
-    pw[(g + 8) * TOK + t * 8 + 2 * c] = acc[t][2];
-    pw[(g + 8) * TOK + t * 8 + 2 * c + 1] = acc[t][3];
-  }
+  if (warp == 1) tmem_alloc(tmem_slot, TCOLS);
+  tc_fence_before();
   __syncthreads();
-  for (int e = threadIdx.x; e < NRG * 16 * TOK; e += kThreads) {
-    const int s = e / (16 * TOK);
-    const int off = e % (16 * TOK);
-    float v = 0.f;
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  TPP_TS(1);
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    auto load_w = [&](int i) {
+      const int s = i % kStages;
+      const int kc = (kb0 + i) * BK;
+      mbar_arrive_expect_tx(&full[s], kStageA + kStageB);
+      if (SWIGLU) {
+        tma_load_2d(sA + s * kStageA, &tm_w, &full[s], kc, out0);
+        tma_load_2d(sA + s * kStageA + kStageA / 2, &tm_w, &full[s], kc, p.N + out0);
+      } else {
+        tma_load_2d(sA + s * kStageA, &tm_w, &full[s], kc, out0);
+      }
+    };
+    const int pre = nk < kStages ? nk : kStages;
+    for (int i = 0; i < pre; ++i) load_w(i);  // weights: independent of the previous kernel
+    pdl_wait();
+    pdl_trigger();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(sB + (i % kStages) * kStageB, &tm_x, &full[i % kStages], (kb0 + i) * BK, 0);
+    for (int i = pre; i < nk && ok; ++i) {
+      const int s = i % kStages;
+      ok = mbar_wait(&empty[s], ((i / kStages) & 1) ^ 1, p.err, 11);
+      if (!ok) break;
+      load_w(i);
+      tma_load_2d(sB + s * kStageB, &tm_x, &full[s], (kb0 + i) * BK, 0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    pdl_wait();
+    constexpr uint32_t idesc = make_idesc_f16(BM, BN, IsBf16<T>::value, 0, 0);
+    for (int i = 0; i < nk && ok; ++i) {
+      const int s = i % kStages;
+      ok = mbar_wait(&full[s], (i / kStages) & 1, p.err, 12);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + s * kStageA);
+      const uint32_t b0 = smem_u32(sB + s * kStageB);
 #pragma unroll
-    for (int w = 0; w < WK; ++w) v += part[(s * WK + w) * 16 * TOK + off];
-    red[e] = v;
+      for (int k = 0; k < BK / 16; ++k) {
+        const uint64_t ad = make_sdesc(a0 + k * 32, 16, 1024, 2);
+        const uint64_t bd = make_sdesc(b0 + k * 32, 16, 1024, 2);
+        tc_mma_f16(tmem, ad, bd, idesc, (i | k) != 0);
+      }
+      tc_commit(&empty[s]);
+    }
+    tc_commit(accum);
+  } else {
+    pdl_wait();
   }
+  __syncwarp();
+
+  // ---------------- accumulator -> registers -> stage ----------------
+  // Without a cluster each thread finishes its own row (output) from
+  // registers.  With a cluster, rank r owns outputs [o0, o1) of the tile:
+  // every rank pushes its partial rows for them into the owner's receive
+  // buffer with remote shared-memory stores (fire-and-forget), and after
+  // one cluster barrier each owner sums what it received.
+  const bool got = mbar_wait(accum, 0, p.err, 13);
+  tc_fence_after();
+  TPP_TS(2);
+  const int row = warp * 32 + lane;  // tile row = TMEM lane
+  const int per = NOUT / csize;       // csize divides NOUT (host picks 1, 2, 4 or 8)
+  const int o0 = crank * per;
+  const T* bias = static_cast<const T*>(p.bias);
+  float v[BN];
+  tmem_ld_row<BN>(tmem + ((uint32_t)(warp * 32) << 16), v);
+  if (!got || nk == 0) {
+#pragma unroll
+    for (int j = 0; j < BN; ++j) v[j] = 0.f;
+  }
+  TPP_TS(3);
   if (csize > 1) {
+    // The receive buffer aliases every rank's TMA ring: a rank may only be
+    // written to once its own MMAs are done, so arrive here and wait below.
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    // recv[src][rowl][RSV]: rows of this rank's slice (gate rows then, for
+    // SwiGLU, the matching up rows), one block of rows per source rank
+    const int rows_per = SWIGLU ? 2 * per : per;
+    const int orow = SWIGLU ? (row % (BM / 2)) : row;   // output index of my row
+    const int owner = orow / per;
+    const int rowl = (orow % per) + ((SWIGLU && row >= BM / 2) ? per : 0);
+    const uint32_t dst = smem_u32(recv) + (uint32_t)(((crank * rows_per + rowl) * RSV) * 4);
+    uint32_t rdst;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"(owner));
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < BN; j += 4)
+      asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + 4 * j),
+                   "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]), "f"(v[j + 3])
+                   : "memory");
     cluster.sync();
-    if (crank == 0) {
-      for (int r = 1; r < csize; ++r) {
-        const float* peer = cluster.map_shared_rank(red, r);
-        for (int e = threadIdx.x; e < NRG * 16 * TOK; e += kThreads) red[e] += peer[e];
+    TPP_TS(4);
+    // token-fastest mapping: conflict-free reads of recv rows and (per + 1 is
+    // odd) conflict-free writes of stage columns
+    for (int e = threadIdx.x; e < per * BN; e += kThreads) {
+      const int t = e % BN, ol = e / BN;
+      float g = 0.f, u = 0.f;
+      for (int r = 0; r < csize; ++r) {
+        g += recv[(r * rows_per + ol) * RSV + t];
+        if (SWIGLU) u += recv[(r * rows_per + per + ol) * RSV + t];
+      }
+      const int n = out0 + o0 + ol;
+      float out = 0.f;
+      if (n < p.N) {
+        if (SWIGLU) {
+          if (bias) { g += to_f32(bias[n]); u += to_f32(bias[p.N + n]); }
+          out = act_silu(g) * u;
+        } else {
+          if (bias) g += to_f32(bias[n]);
+          out = apply_act(p.act, g);
+        }
+      }
+      stage[t * (per + 1) + ol] = out;
+    }
+  } else {
+    TPP_TS(4);
+    if (SWIGLU) {
+      // up rows (warps 2, 3) hand their values to the gate rows via smem
+      if (row >= BM / 2) {
+#pragma unroll
+        for (int j = 0; j < BN; ++j) recv[(row - BM / 2) * RS + j] = v[j];
+      }
+      __syncthreads();
+      if (row < BM / 2) {
+        const int n = out0 + row;
+        const float bg = (bias && n < p.N) ? to_f32(bias[n]) : 0.f;
+        const float bu = (bias && n < p.N) ? to_f32(bias[p.N + n]) : 0.f;
+#pragma unroll
+        for (int j = 0; j < BN; ++j)
+          stage[j * (per + 1) + row] = act_silu(v[j] + bg) * (recv[row * RS + j] + bu);
+      }
+    } else {
+      const int n = out0 + row;
+      const float bb = (bias && n < p.N) ? to_f32(bias[n]) : 0.f;
+      const int act = p.act;
+#pragma unroll
+      for (int j = 0; j < BN; ++j) stage[j * (per + 1) + row] = apply_act(act, v[j] + bb);
+    }
+  }
+  TPP_TS(5);
+  __syncthreads();
+  TPP_TS(6);
+
+  // ---------------- coalesced store (+ residual) ----------------
+  {
+    const T* res = static_cast<const T*>(p.residual);
+    T* Y = static_cast<T*>(p.y);
+    const int mt = p.M < BN ? p.M : BN;
+    const int chunks = per / 8;  // 8 outputs = 16 bytes per store
+    for (int e = threadIdx.x; e < mt * chunks; e += kThreads) {
+      const int t = e / chunks, ch = e % chunks;
+      const int n0 = out0 + o0 + ch * 8;
+      if (n0 >= p.N) continue;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = stage[t * (per + 1) + ch * 8 + j];
+      T* yr = Y + (int64_t)t * p.ldy;
+      const T* rr = res ? res + (int64_t)t * p.ldy : nullptr;
+      if (p.vec_ok && n0 + 8 <= p.N) {
+        if (rr) {
+          float rf[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(rr + n0), rf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += rf[j];
+        }
+        *reinterpret_cast<uint4*>(yr + n0) = pack8<T>(o);
+      } else {
+        for (int j = 0; j < 8 && n0 + j < p.N; ++j) {
+          float a = o[j];
+          if (rr) a += to_f32(rr[n0 + j]);
+          yr[n0 + j] = from_f32<T>(a);
+        }
       }
     }
-    cluster.sync();  // peers keep their shared memory alive until rank 0 has read it
-    if (crank != 0) return;
-  } else {
-    __syncthreads();
   }
-
-  // ---- epilogue (rank 0): token-major so 16 consecutive rows are contiguous ----
-  const T* bias = static_cast<const T*>(p.bias);
-  const T* res = static_cast<const T*>(p.residual);
-  T* Y = static_cast<T*>(p.y);
-  for (int e = threadIdx.x; e < 16 * TOK; e += kThreads) {
-    const int tok = e / 16, r = e % 16;
-    const int n = blockIdx.x * 16 + r;
-    if (tok >= p.M || n >= p.N) continue;
-    float v = red[r * TOK + tok];
-    if (NRG == 2) {
-      float u = red[16 * TOK + r * TOK + tok];
-      if (bias) { v += to_f32(bias[n]); u += to_f32(bias[p.N + n]); }
-      v = act_silu(v) * u;
-    } else {
-      if (bias) v += to_f32(bias[n]);
-      v = apply_act(p.act, v);
-    }
-    if (res) v += to_f32(res[(int64_t)tok * p.ldy + n]);
-    Y[(int64_t)tok * p.ldy + n] = from_f32<T>(v);
+#ifdef TPP_DEBUG_STAMPS
+  TPP_TS(7);
+  if (threadIdx.x == 0) {
+    const int id = blockIdx.y * gridDim.x + blockIdx.x;
+    for (int i = 0; i < 8; ++i) g_dbg_stamps[8 * id + i] = stamps[i];
   }
+#endif
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TCOLS);
 }
 
-template <typename T, int NRG, int MT>
-int launch_linear_decode(const LinearArgs& a0, cudaStream_t st) {
-  LinearArgs a = a0;
-  const int nrb = (a.N + 15) / 16;
-  const int nchunks = (a.K + 63) / 64;
-  constexpr int WK = kWarps / NRG;
-  // Enough CTAs to keep every SM streaming, but each split gets >= 1 chunk.
-  const int target = 2 * num_sms();
-  int ck = (target + nrb - 1) / nrb;
-  ck = ck < 1 ? 1 : (ck > 8 ? 8 : ck);
-  while (ck > 1 && ck * WK > nchunks) --ck;
-  const int splits = ck * WK;
-  a.chunks_per_split = (nchunks + splits - 1) / splits;
-  const size_t smem = (size_t)(kWarps * 16 * MT * 8 + NRG * 16 * MT * 8) * sizeof(float);
-
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)nrb, (unsigned)ck, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)ck;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // 256-bit weight loads need 32-byte aligned rows.
-  const bool v8 = (a.K % 16 == 0) && ((reinterpret_cast<uintptr_t>(a.w) & 31u) == 0);
-  cudaError_t e = v8 ? cudaLaunchKernelEx(&cfg, linear_decode_kernel<T, NRG, MT, true>, a)
-                     : cudaLaunchKernelEx(&cfg, linear_decode_kernel<T, NRG, MT, false>, a);
-  if (e != cudaSuccess) {
-    set_error(std::string("linear_decode_kernel: ") + cudaGetErrorString(e));
-    return TPP_ERR_LAUNCH;
+template <typename T, int BN, bool SW>
+int launch_skinny(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int dtype,
+                  cudaStream_t st) {
+  constexpr int NOUT = SW ? BM / 2 : BM;
+  CUtensorMap tw, tx;
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)(SW ? 2 * (int64_t)a.N : a.N)};
+    const uint64_t strides[1] = {(uint64_t)a.K * 2};
+    const uint32_t box[2] = {BK, (uint32_t)(SW ? BM / 2 : BM)};
+    const int rc = make_tmap(&tw, w, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
   }
-  return check_launch("linear_decode_kernel");
+  {
+    const uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.M};
+    const uint64_t strides[1] = {(uint64_t)ldx * 2};
+    const uint32_t box[2] = {BK, (uint32_t)BN};
+    const int rc = make_tmap(&tx, x, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  }
+  const int tiles = (a.N + NOUT - 1) / NOUT;
+  const int nkb = (a.K + BK - 1) / BK;
+  // Enough CTAs for two per SM; every split keeps >= 2 k-blocks.
+  int ks = (2 * num_sms() + tiles - 1) / tiles;
+  int maxks = nkb / 2 > 0 ? nkb / 2 : 1;
+  if (maxks > 8) maxks = 8;
+  ks = ks < 1 ? 1 : (ks > maxks ? maxks : ks);
+  // cluster size 1, 2, 4 or 8 (it must divide the tile's outputs for the
+  // reduce-scatter); a split may end up with fewer k-blocks than others
+  ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
+  a.kb_per_split = (nkb + ks - 1) / ks;
+  auto kern = linear_skinny_kernel<T, BN, SW>;
+  constexpr size_t smem = smem_bytes<BN>();
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      set_error("linear_skinny_kernel: cannot reserve shared memory");
+      return TPP_ERR_LAUNCH;
+    }
+    configured |= bit;
+  }
+  return launch("linear_skinny_kernel", kern, dim3((unsigned)tiles, (unsigned)ks, 1),
+                dim3(kThreads), smem, st, (unsigned)ks, tw, tx, a);
 }
 
 template <typename T>
-int linear_decode_dispatch(const LinearArgs& a, cudaStream_t st) {
+int skinny_dispatch(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int dtype,
+                    cudaStream_t st) {
   const bool sw = a.act == TPP_ACT_SWIGLU;
-  auto go = [&](auto mt) -> int {
-    constexpr int MT = decltype(mt)::value;
-    return sw ? launch_linear_decode<T, 2, MT>(a, st) : launch_linear_decode<T, 1, MT>(a, st);
-  };
-  if (a.M <= 8) return go(std::integral_constant<int, 1>{});
-  if (a.M <= 16) return go(std::integral_constant<int, 2>{});
-  if (a.M <= 32) return go(std::integral_constant<int, 4>{});
-  return go(std::integral_constant<int, 8>{});
+  if (a.M <= 16)
+    return sw ? launch_skinny<T, 16, true>(x, ldx, w, a, dtype, st)
+              : launch_skinny<T, 16, false>(x, ldx, w, a, dtype, st);
+  if (a.M <= 32)
+    return sw ? launch_skinny<T, 32, true>(x, ldx, w, a, dtype, st)
+              : launch_skinny<T, 32, false>(x, ldx, w, a, dtype, st);
+  return sw ? launch_skinny<T, 64, true>(x, ldx, w, a, dtype, st)
+            : launch_skinny<T, 64, false>(x, ldx, w, a, dtype, st);
 }
 
 }  // namespace
+
+#ifdef TPP_DEBUG_STAMPS
+extern "C" void tpp_debug_stamps(unsigned long long* host, int n) {
+  cudaMemcpyFromSymbol(host, g_dbg_stamps, sizeof(unsigned long long) * n);
+}
+#endif
 
 // Entry used by tpp_linear (linear.cu) for M <= 64.
 int linear_decode(const void* x, int64_t ldx, const void* w, const void* bias,
                   const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                   int act, int dtype, cudaStream_t st) {
-  LinearArgs a;
-  a.x = x; a.ldx = ldx; a.w = w; a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
-  a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act; a.chunks_per_split = 0;
-  return TPP_DISPATCH_HALF(dtype, T, [&] { return linear_decode_dispatch<T>(a, st); });
+  SkinnyArgs a;
+  a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
+  a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act; a.kb_per_split = 0;
+  a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned16(y) && (!residual || aligned16(residual));
+  a.err = device_error_flag();
+  return TPP_DISPATCH_HALF(dtype, T, [&] { return skinny_dispatch<T>(x, ldx, w, a, dtype, st); });
 }
 
 }  // namespace tpp

@@ -81,6 +81,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barrier init, TMEM allocation and descriptor prefetch above overlap the
+  // previous kernel; everything below reads its outputs.
+  pdl_wait();
+  pdl_trigger();
 
   bool ok = true;
   if (warp == 0 && lane == 0) {
@@ -223,8 +227,7 @@ int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const
       set_error("linear_tc_kernel: cannot reserve shared memory");
       return (int)TPP_ERR_LAUNCH;
     }
-    kern<<<grid, kThreads, kSmem, st>>>(tx, tw, a);
-    return check_launch("linear_tc_kernel");
+    return launch("linear_tc_kernel", kern, dim3(grid), dim3(kThreads), kSmem, st, 0, tx, tw, a);
   });
 }
 

@@ -14,6 +14,8 @@ template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, int64_t ld,
                                                       int64_t V, int64_t* __restrict__ out,
                                                       bool vec) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int64_t si[32];
   const T* row = x + (int64_t)blockIdx.x * ld;
@@ -65,6 +67,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ ids, int64_t T_,
                                                         const T* __restrict__ table, int64_t V,
                                                         int64_t D, T* __restrict__ out, bool vec) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t per_row = vec ? D / 8 : D;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= T_ * per_row) return;
@@ -82,6 +86,8 @@ __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restric
 __global__ void decode_advance_kernel(const int64_t* __restrict__ next, int64_t* __restrict__ out_ids,
                                       int64_t ld_out, int32_t* __restrict__ positions,
                                       int32_t* __restrict__ seqlens, int64_t B, int64_t cap) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int32_t p = positions[b] + 1;
@@ -102,9 +108,8 @@ extern "C" int tpp_decode_advance(const int64_t* next_tokens, int64_t* out_ids, 
   TPP_REQUIRE(B >= 0 && (out_ids == nullptr || (ld_out >= out_cap && out_cap >= 0)),
               TPP_ERR_SHAPE, "bad sizes");
   if (B == 0) return TPP_OK;
-  decode_advance_kernel<<<(unsigned)((B + 127) / 128), 128, 0, as_stream(stream)>>>(
+  return launch("decode_advance_kernel", decode_advance_kernel, dim3((unsigned)((B + 127) / 128)), dim3(128), 0, as_stream(stream), 0, 
       next_tokens, out_ids, ld_out, positions, seqlens, B, out_cap);
-  return check_launch("decode_advance_kernel");
 }
 
 extern "C" int tpp_argmax(const void* logits, int64_t ld, int64_t B, int64_t V, int64_t* out,
@@ -116,16 +121,14 @@ extern "C" int tpp_argmax(const void* logits, int64_t ld, int64_t B, int64_t V, 
   auto go = [&](auto tag) -> int {
     using T = decltype(tag);
     const bool vec = (ld % 8 == 0) && aligned16(logits) && sizeof(T) == 2;
-    argmax_kernel<T><<<(unsigned)B, 1024, 0, as_stream(stream)>>>((const T*)logits, ld, V, out,
+    return launch("argmax_kernel", argmax_kernel<T>, dim3((unsigned)B), dim3(1024), 0, as_stream(stream), 0, (const T*)logits, ld, V, out,
                                                                   vec);
-    return check_launch("argmax_kernel");
   };
   if (dtype == TPP_F16) return go(__half());
   if (dtype == TPP_BF16) return go(__nv_bfloat16());
   if (dtype == TPP_F32) {
-    argmax_kernel<float><<<(unsigned)B, 1024, 0, as_stream(stream)>>>((const float*)logits, ld, V,
+    return launch("argmax_kernel", argmax_kernel<float>, dim3((unsigned)B), dim3(1024), 0, as_stream(stream), 0, (const float*)logits, ld, V,
                                                                       out, false);
-    return check_launch("argmax_kernel");
   }
   set_error("tpp_argmax: dtype must be f16, bf16 or f32");
   return TPP_ERR_DTYPE;
@@ -140,8 +143,7 @@ extern "C" int tpp_embedding(const int64_t* ids, int64_t T_, const void* table, 
   return TPP_DISPATCH_HALF(dtype, T, [&] {
     const bool vec = D % 8 == 0 && aligned16(table) && aligned16(out);
     const int64_t total = T_ * (vec ? D / 8 : D);
-    embedding_kernel<T><<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(
+    return launch("embedding_kernel", embedding_kernel<T>, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, as_stream(stream), 0, 
         ids, T_, (const T*)table, V, D, (T*)out, vec);
-    return check_launch("embedding_kernel");
   });
 }

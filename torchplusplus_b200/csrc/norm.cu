@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(
     const T* __restrict__ x, int64_t ldx, T* res, const T* __restrict__ w,
     const T* __restrict__ b, T* __restrict__ y, int64_t ldy, int64_t rows, int cols,
     float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int groups = blockDim.x / G;
   const int64_t row = (int64_t)blockIdx.x * groups + threadIdx.x / G;
   const int lane = threadIdx.x % G;
@@ -109,6 +111,8 @@ __global__ void __launch_bounds__(256) norm_rows_generic_kernel(
     const T* __restrict__ x, int64_t ldx, T* res, const T* __restrict__ w,
     const T* __restrict__ b, T* __restrict__ y, int64_t ldy, int64_t rows, int cols,
     float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
@@ -156,9 +160,8 @@ int launch_rows(const T* x, int64_t ldx, T* res, const T* w, const T* b, T* y, i
   const int threads = 256;
   const int groups = threads / G;
   const int64_t grid = (rows + groups - 1) / groups;
-  norm_rows_kernel<T, G, NV, MODE><<<(unsigned)grid, threads, 0, st>>>(x, ldx, res, w, b, y, ldy,
+  return launch("norm_rows_kernel", norm_rows_kernel<T, G, NV, MODE>, dim3((unsigned)grid), dim3(threads), 0, st, 0, x, ldx, res, w, b, y, ldy,
                                                                        rows, cols, eps);
-  return check_launch("norm_rows_kernel");
 }
 
 template <typename T, int MODE>
@@ -186,9 +189,8 @@ int norm_dispatch(const void* xv, int64_t ldx, void* resv, const void* wv, const
     return launch_rows<T, 32, 16, MODE>(x, ldx, res, w, b, y, ldy, rows, (int)cols, eps, st);
   }
   TPP_REQUIRE(rows <= 0x7fffffffLL, TPP_ERR_SHAPE, "too many rows for the generic path");
-  norm_rows_generic_kernel<T, MODE><<<(unsigned)rows, 256, 0, st>>>(x, ldx, res, w, b, y, ldy, rows,
+  return launch("norm_rows_generic_kernel", norm_rows_generic_kernel<T, MODE>, dim3((unsigned)rows), dim3(256), 0, st, 0, x, ldx, res, w, b, y, ldy, rows,
                                                                     (int)cols, eps);
-  return check_launch("norm_rows_generic_kernel");
 }
 
 }  // namespace

@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(
     const T* __restrict__ x, int64_t sb, int64_t sh, int64_t ss, const CS* __restrict__ cosp,
     const CS* __restrict__ sinp, int64_t cs_stride, T* __restrict__ out, int64_t H, int64_t S,
     int D, int64_t pos_offset, int64_t total) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int chunks = D >> 4;  // 8-element chunks per half
@@ -81,6 +83,8 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(
     const T* __restrict__ x, int64_t sb, int64_t sh, int64_t ss, const CS* __restrict__ cosp,
     const CS* __restrict__ sinp, int64_t cs_stride, T* __restrict__ out, int64_t H, int64_t S,
     int D, int64_t pos_offset, int64_t total) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int half = D >> 1;
@@ -111,15 +115,13 @@ int rope_launch(const T* x, int64_t sb, int64_t sh, int64_t ss, const CS* c, con
   if (vec) {
     const int64_t total = rows * (D / 16);
     const int64_t grid = (total + 255) / 256;
-    rope_vec_kernel<T, CS><<<(unsigned)grid, 256, 0, st>>>(x, sb, sh, ss, c, s, cs_stride, out, H,
+    return launch("rope_vec_kernel", rope_vec_kernel<T, CS>, dim3((unsigned)grid), dim3(256), 0, st, 0, x, sb, sh, ss, c, s, cs_stride, out, H,
                                                           S, (int)D, pos_offset, total);
-    return check_launch("rope_vec_kernel");
   }
   const int64_t total = rows * (D / 2);
   const int64_t grid = (total + 255) / 256;
-  rope_scalar_kernel<T, CS><<<(unsigned)grid, 256, 0, st>>>(x, sb, sh, ss, c, s, cs_stride, out,
+  return launch("rope_scalar_kernel", rope_scalar_kernel<T, CS>, dim3((unsigned)grid), dim3(256), 0, st, 0, x, sb, sh, ss, c, s, cs_stride, out,
                                                            H, S, (int)D, pos_offset, total);
-  return check_launch("rope_scalar_kernel");
 }
 
 template <typename T>
@@ -157,6 +159,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_cache_kernel(
     const CS* __restrict__ sinp, int64_t cs_stride, const int32_t* __restrict__ positions,
     T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache, int64_t c_sb,
     int64_t c_sh, int64_t c_ss, int64_t B, int64_t S, int Hq, int Hkv, int D) {
+  pdl_wait();
+  pdl_trigger();
   const int groups_per_block = blockDim.x / G;
   const int heads = Hq + 2 * Hkv;
   const int64_t item = (int64_t)blockIdx.x * groups_per_block + threadIdx.x / G;
@@ -224,6 +228,8 @@ __global__ void __launch_bounds__(256) kv_append_kernel(
     int64_t v_sb, int64_t v_sh, int64_t v_ss, T* __restrict__ kc, T* __restrict__ vc,
     int64_t c_sb, int64_t c_sh, int64_t c_ss, int64_t Hkv, int64_t S, int D, int64_t start_pos,
     const int32_t* __restrict__ positions, int64_t total, bool vec) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total) return;
   const int per_row = vec ? D / 8 : D;
@@ -299,10 +305,9 @@ static int qnrc_launch(const void* qkv, int64_t ld, const void* qn, const void* 
     constexpr int G = decltype(g_tag)::value;
     const int per_block = 256 / G;
     const int64_t grid = (total + per_block - 1) / per_block;
-    qk_norm_rope_cache_kernel<T, CS, G><<<(unsigned)grid, 256, 0, st>>>(
+    return launch("qk_norm_rope_cache_kernel", qk_norm_rope_cache_kernel<T, CS, G>, dim3((unsigned)grid), dim3(256), 0, st, 0, 
         (const T*)qkv, ld, (const T*)qn, (const T*)kn, eps, (const CS*)c, (const CS*)s, cs_stride,
         pos, (T*)q_out, (T*)kc, (T*)vc, c_sb, c_sh, c_ss, B, S, (int)Hq, (int)Hkv, (int)D);
-    return check_launch("qk_norm_rope_cache_kernel");
   };
   switch (D) {
     case 16: return go(std::integral_constant<int, 2>{});
@@ -373,9 +378,8 @@ extern "C" int tpp_kv_append(const void* k, int64_t k_sb, int64_t k_sh, int64_t 
     const int64_t total = B * Hkv * S * (vec ? D / 8 : D);
     if (total == 0) return (int)TPP_OK;
     const int64_t grid = (total + 255) / 256;
-    kv_append_kernel<T><<<(unsigned)grid, 256, 0, as_stream(stream)>>>(
+    return launch("kv_append_kernel", kv_append_kernel<T>, dim3((unsigned)grid), dim3(256), 0, as_stream(stream), 0, 
         (const T*)k, k_sb, k_sh, k_ss, (const T*)v, v_sb, v_sh, v_ss, (T*)k_cache, (T*)v_cache,
         c_sb, c_sh, c_ss, Hkv, S, (int)D, start_pos, positions, total, vec);
-    return check_launch("kv_append_kernel");
   });
 }

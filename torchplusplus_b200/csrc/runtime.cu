@@ -1,5 +1,6 @@
 // Library-level plumbing of the C-ABI: error messages, version, launch count.
 #include <atomic>
+#include <cstdlib>
 #include "common.cuh"
 
 namespace tpp {
@@ -9,6 +10,14 @@ static std::atomic<uint64_t> g_launches{0};
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("TPP_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
