@@ -20,7 +20,8 @@
 //    merges the splits.
 #include <math.h>
 #include <mutex>
-#include "common.cuh"
+#include "tc_common.cuh"
+#include "attn_decode.cuh"
 
 namespace tpp {
 
@@ -266,6 +267,13 @@ int decode_launch(DecodeArgs& a, int64_t B, cudaStream_t st) {
 }  // namespace
 
 int64_t attn_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t range, int64_t D) {
+  if (D == 64 || D == 128) {
+    // tensor-core path: up to 8 splits merge inside a cluster, more go
+    // through the workspace
+    const int s = decode_mma_splits(B, Hq, Hkv, range);
+    if (s <= 8) return 0;
+    return B * Hq * (int64_t)s * (D + 1) * (int64_t)sizeof(float) + 256;
+  }
   const int s = attn_decode_num_splits(B, Hq, Hkv, range);
   if (s <= 1) return 0;
   return B * Hq * (int64_t)s * (D + 1) * (int64_t)sizeof(float) + 256;
@@ -292,6 +300,40 @@ int attn_decode_run(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cac
   if (B == 0) return TPP_OK;
   int64_t range = max_seqlen;
   if (window_left >= 0 && window_left + 1 < range) range = window_left + 1;
+  if (D == 64 || D == 128) {
+    TPP_REQUIRE(c_ss == D, TPP_ERR_ALIGN, "cache rows must be contiguous (seq stride == head dim)");
+    DecMmaArgs m;
+    m.q = q; m.q_sb = q_sb; m.q_sh = q_sh;
+    m.o = o; m.o_sb = o_sb; m.o_sh = o_sh;
+    m.seqlens = seqlens; m.max_seqlen = max_seqlen;
+    m.Hq = (int)Hq; m.Hkv = (int)Hkv; m.G = (int)(Hq / Hkv); m.passes = 1;
+    m.window_left = window_left;
+    m.scale_log2 = scale * kLog2e;
+    m.splits = decode_mma_splits(B, Hq, Hkv, range);
+    m.cluster = 1;
+    m.ws_o = nullptr; m.ws_lse = nullptr;
+    m.err = device_error_flag();
+    if (m.splits > 8) {
+      const int64_t need = attn_decode_workspace_bytes(B, Hq, Hkv, range, D);
+      TPP_REQUIRE(ws != nullptr && ws_bytes >= need, TPP_ERR_WORKSPACE,
+                  "workspace too small: need " + std::to_string(need) + " bytes");
+      TPP_REQUIRE(aligned16(ws), TPP_ERR_ALIGN, "workspace must be 16-byte aligned");
+      m.ws_o = static_cast<float*>(ws);
+      m.ws_lse = m.ws_o + B * Hq * (int64_t)m.splits * D;
+    }
+    int rc = decode_mma_launch(m, k_cache, v_cache, c_sb, c_sh, c_ss, B, D, dtype, st);
+    if (rc != TPP_OK || m.splits <= 8) return rc;
+    DecodeArgs a;
+    a.o = o; a.o_sb = o_sb; a.o_sh = o_sh; a.Hq = (int)Hq; a.num_splits = m.splits;
+    a.ws_o = m.ws_o; a.ws_lse = m.ws_lse;
+    const int64_t blocks = (B * Hq * 32 + 255) / 256;
+    return TPP_DISPATCH_HALF(dtype, T, [&] {
+      return D == 64 ? launch("decode_combine_kernel", decode_combine_kernel<T, 64>,
+                              dim3((unsigned)blocks), dim3(256), 0, st, 0u, a, B)
+                     : launch("decode_combine_kernel", decode_combine_kernel<T, 128>,
+                              dim3((unsigned)blocks), dim3(256), 0, st, 0u, a, B);
+    });
+  }
   DecodeArgs a;
   a.q = q; a.q_sb = q_sb; a.q_sh = q_sh;
   a.kc = k_cache; a.vc = v_cache; a.c_sb = c_sb; a.c_sh = c_sh; a.c_ss = c_ss;

@@ -1,0 +1,406 @@
+// Decode attention on tensor cores: one query token per sequence, the G query
+// heads of a KV group stacked as the rows of m16n8k16 MMA tiles, K/V streamed
+// by TMA through a shared-memory ring, split-KV partials merged inside a
+// thread-block cluster over distributed shared memory.
+//
+// Semantics as decode_attn_kernel (attn_decode.cu): keys [p - window_left, p]
+// of a BHSD cache, p = seqlen - 1; query head h reads kv head h / G (the
+// repeat_interleave of torchpp/attention/gqa.py:120-121, not materialised).
+//
+// Design (HBM-bound on the cache):
+//  * grid (split, kv_head x head_pass, batch), cluster (splits, 1, 1) when
+//    there are at most 8 splits.  A CTA streams one slice of one kv head's
+//    key range once for all (up to 16) query heads of the group.
+//  * Thread 0 issues 4-D TMA loads (128-byte swizzle, no multicast) of
+//    64-key K and V tiles into a kStages ring (full/empty mbarriers, bounded
+//    waits).  Each of the 4 warps takes 16 keys of every tile:
+//    S = Q.K^T (D/16 x 2 MMAs), fp32 online softmax in the exp2 domain,
+//    O += P.V (D/8 MMAs); fragments come from ldmatrix on the swizzled tiles.
+//  * The 4 warps merge in shared memory; the splits then merge at cluster
+//    rank 0 (peers push (o, lse) with 16-byte remote stores), or -- beyond 8
+//    splits -- write (o, lse) partials to the caller's workspace for
+//    decode_combine_kernel.
+#include <math.h>
+#include <cooperative_groups.h>
+#include "mma_common.cuh"
+#include "tc_common.cuh"
+#include "attn_decode.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace tpp {
+
+
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int KT = 64;      // keys per tile
+constexpr int kStages = 3;
+constexpr int QR = 16;      // query-head rows per CTA (MMA M)
+
+// Address of 16-byte chunk `chunk` of row r in a TMA 128B-swizzled tile made of
+// 64-element-wide boxes stacked along the row (box b holds chunks 8b..8b+7).
+__device__ __forceinline__ uint32_t sw_addr(uint32_t base, int box_rows, int r, int chunk) {
+  return base + (uint32_t)((chunk >> 3) * box_rows * 128 + r * 128 + (((chunk & 7) ^ (r & 7)) << 4));
+}
+
+template <int D>
+struct DecSmem {
+  static constexpr uint32_t kTile = KT * D * 2;                 // one K or V tile
+  static constexpr uint32_t kRing = kStages * 2 * kTile;
+  static constexpr uint32_t kWc = 4 * QR * (D + 2) * 4;         // per-warp (m, l, o)
+  static constexpr uint32_t kRecv = 8 * QR * (D + 4) * 4;       // per-split (o, lse)
+  static constexpr uint32_t kWork = (kRing > kWc + kRecv) ? kRing : (kWc + kRecv);
+  static constexpr uint32_t kQ = QR * D * 2;
+  static constexpr size_t kBytes = 1024 + kWork + kQ + 128;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads) decode_mma_kernel(
+    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+    DecMmaArgs p) {
+  using SM = DecSmem<D>;
+  constexpr int NCH = D / 8;  // 16-byte chunks per row
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* ring = smem;
+  uint8_t* sq = smem + SM::kWork;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sq + SM::kQ);
+  uint64_t* empty = full + kStages;
+  float* wc = reinterpret_cast<float*>(smem);                 // after the loop
+  float* recv = reinterpret_cast<float*>(smem + SM::kWc);     // after the loop
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / p.passes;
+  const int pass = blockIdx.y % p.passes;
+  const int b = blockIdx.z;
+  const int h0 = kvh * p.G + pass * QR;
+  const int nh = min(QR, p.G - pass * QR);
+
+  if (tid == 0) {
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Sequence lengths, the cache rows of this step and q come from earlier
+  // kernels of the step.
+  pdl_wait();
+  pdl_trigger();
+
+  const int64_t L = p.seqlens ? (int64_t)p.seqlens[b] : p.max_seqlen;
+  int64_t lo = 0;
+  if (p.window_left >= 0) lo = max((int64_t)0, L - 1 - p.window_left);
+  const int64_t n = L > lo ? L - lo : 0;
+  int64_t per = (n + p.splits - 1) / p.splits;
+  per = (per + KT - 1) / KT * KT;
+  const int64_t k0 = lo + (int64_t)split * per;
+  const int64_t k1 = min(L, k0 + per);
+  const int ntiles = k1 > k0 ? (int)((k1 - k0 + KT - 1) / KT) : 0;
+
+  auto issue = [&](int i) {
+    const int s = i % kStages;
+    uint8_t* kd = ring + s * 2 * SM::kTile;
+    uint8_t* vd = kd + SM::kTile;
+    const int key = (int)(k0 + (int64_t)i * KT);
+    mbar_arrive_expect_tx(&full[s], 2 * SM::kTile);
+#pragma unroll
+    for (int bx = 0; bx < D / 64; ++bx) {
+      tma_load_4d(kd + bx * KT * 128, &tm_k, &full[s], bx * 64, key, kvh, b);
+      tma_load_4d(vd + bx * KT * 128, &tm_v, &full[s], bx * 64, key, kvh, b);
+    }
+  };
+  if (tid == 0) {
+    for (int i = 0; i < ntiles && i < kStages; ++i) issue(i);
+  }
+
+  // ---- Q rows (heads h0 .. h0+nh-1, zero padding) -> swizzled smem -> A fragments ----
+  const T* Q = static_cast<const T*>(p.q) + b * p.q_sb;
+  const uint32_t sq_a = smem_u32(sq);
+  for (int e = tid; e < QR * NCH; e += kThreads) {
+    const int r = e / NCH, ch = e % NCH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nh) v = __ldg(reinterpret_cast<const uint4*>(Q + (int64_t)(h0 + r) * p.q_sh) + ch);
+    *reinterpret_cast<uint4*>(sq + (sw_addr(sq_a, QR, r, ch) - sq_a)) = v;
+  }
+  __syncthreads();
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+    ldsm_x4(sw_addr(sq_a, QR, r, ks * 2 + (lane >> 4)), qf[ks]);
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  bool ok = true;
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % kStages;
+    // refill the stage released one iteration ago
+    if (tid == 0 && i >= 1 && i - 1 + kStages < ntiles) {
+      const int sp = (i - 1) % kStages;
+      ok = mbar_wait(&empty[sp], ((i - 1) / kStages) & 1, p.err, 21) && ok;
+      if (ok) issue(i - 1 + kStages);
+    }
+    if (!mbar_wait(&full[s], (i / kStages) & 1, p.err, 22)) { ok = false; break; }
+    const uint32_t kb = smem_u32(ring + s * 2 * SM::kTile);
+    const uint32_t vb = kb + SM::kTile;
+    const int kr0 = warp * 16;  // this warp's 16 keys of the tile
+
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t bf[4];
+      const int r = kr0 + (lane & 7) + (lane >> 4) * 8;
+      ldsm_x4(sw_addr(kb, KT, r, ks * 2 + ((lane >> 3) & 1)), bf);
+      mma<T>(sc[0], qf[ks], bf[0], bf[1]);
+      mma<T>(sc[1], qf[ks], bf[2], bf[3]);
+    }
+    const int64_t kbase = k0 + (int64_t)i * KT + kr0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t key = kbase + j * 8 + 2 * c + (e & 1);
+        sc[j][e] = key < k1 ? sc[j][e] * p.scale_log2 : -INFINITY;
+      }
+    float corr[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float mx = fmaxf(m_r[hr], fmaxf(fmaxf(sc[0][2 * hr], sc[0][2 * hr + 1]),
+                                      fmaxf(sc[1][2 * hr], sc[1][2 * hr + 1])));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      corr[hr] = (mx == -INFINITY) ? 1.f : exp2f(m_r[hr] - mx);
+      m_r[hr] = mx;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = sc[j][2 * hr + e];
+          const float pv = (v == -INFINITY) ? 0.f : exp2f(v - mx);
+          sc[j][2 * hr + e] = pv;
+          sum += pv;
+        }
+      l_r[hr] = l_r[hr] * corr[hr] + sum;
+    }
+#pragma unroll
+    for (int d = 0; d < D / 8; ++d) {
+      o[d][0] *= corr[0]; o[d][1] *= corr[0];
+      o[d][2] *= corr[1]; o[d][3] *= corr[1];
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<T>(sc[0][0], sc[0][1]);
+    pa[1] = pack2<T>(sc[0][2], sc[0][3]);
+    pa[2] = pack2<T>(sc[1][0], sc[1][1]);
+    pa[3] = pack2<T>(sc[1][2], sc[1][3]);
+#pragma unroll
+    for (int dp = 0; dp < D / 16; ++dp) {
+      uint32_t bf[4];
+      const int r = kr0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4_t(sw_addr(vb, KT, r, dp * 2 + (lane >> 4)), bf);
+      mma<T>(o[2 * dp], pa, bf[0], bf[1]);
+      mma<T>(o[2 * dp + 1], pa, bf[2], bf[3]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- merge the 4 warps (rows g, g+8 of each; l is quad-partial) ----
+  if (p.cluster && p.splits > 1)
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  __syncthreads();  // every warp is done with the ring
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float l = l_r[hr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int r = g + hr * 8;
+    float* base = wc + (warp * QR + r) * (D + 2);
+    if (c == 0) { base[0] = m_r[hr]; base[1] = l; }
+#pragma unroll
+    for (int d = 0; d < D / 8; ++d) {
+      base[2 + d * 8 + 2 * c] = o[d][2 * hr];
+      base[2 + d * 8 + 2 * c + 1] = o[d][2 * hr + 1];
+    }
+  }
+  __syncthreads();
+  // CTA partial for row r: normalised o (fp32) and lse (log2 domain) in the
+  // receive slot of this split (cluster mode: slots 0..7 = cluster ranks;
+  // otherwise slot 0)
+  const int slot = (p.cluster && p.splits > 1) ? split : 0;
+  for (int e = tid; e < nh * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wc[(w * QR + r) * (D + 2)]);
+    float Ls = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float* bw = wc + (w * QR + r) * (D + 2);
+        const float sc = bw[0] == -INFINITY ? 0.f : exp2f(bw[0] - M);
+        Ls += bw[1] * sc;
+        O += bw[2 + d] * sc;
+      }
+    }
+    const float on = Ls > 0.f ? O / Ls : 0.f;
+    const float lse = Ls > 0.f ? M + log2f(Ls) : -INFINITY;
+    recv[(slot * QR + r) * (D + 4) + 4 + d] = on;
+    if (d == 0) recv[(slot * QR + r) * (D + 4)] = lse;
+  }
+  __syncthreads();
+
+  if (p.splits == 1) {
+    T* out = static_cast<T*>(p.o) + b * p.o_sb;
+    for (int e = tid; e < nh * D; e += kThreads) {
+      const int r = e / D, d = e % D;
+      out[(int64_t)(h0 + r) * p.o_sh + d] = from_f32<T>(recv[r * (D + 4) + 4 + d]);
+    }
+    return;
+  }
+  if (!p.cluster) {
+    for (int e = tid; e < nh * D; e += kThreads) {
+      const int r = e / D, d = e % D;
+      const int64_t wslot = ((int64_t)b * p.Hq + h0 + r) * p.splits + split;
+      p.ws_o[wslot * D + d] = recv[r * (D + 4) + 4 + d];
+      if (d == 0) p.ws_lse[wslot] = recv[r * (D + 4)];
+    }
+    return;
+  }
+  // ---- cluster merge at rank 0 ----
+  cg::cluster_group cluster = cg::this_cluster();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (split != 0) {
+    const uint32_t base = smem_u32(recv) + (uint32_t)((split * QR) * (D + 4) * 4);
+    uint32_t rbase;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbase) : "r"(base), "r"(0));
+    for (int e = tid; e < nh * (D + 4) / 4; e += kThreads) {
+      const float4 v = *reinterpret_cast<const float4*>(recv + (split * QR) * (D + 4) + e * 4);
+      asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rbase + 16 * e),
+                   "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                   : "memory");
+    }
+  }
+  cluster.sync();
+  if (split != 0) return;
+  T* out = static_cast<T*>(p.o) + b * p.o_sb;
+  for (int e = tid; e < nh * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, recv[(sp * QR + r) * (D + 4)]);
+    float W = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int sp = 0; sp < p.splits; ++sp) {
+        const float* bs = recv + (sp * QR + r) * (D + 4);
+        const float w = bs[0] == -INFINITY ? 0.f : exp2f(bs[0] - M);
+        W += w;
+        O += w * bs[4 + d];
+      }
+    }
+    out[(int64_t)(h0 + r) * p.o_sh + d] = from_f32<T>(W > 0.f ? O / W : 0.f);
+  }
+  (void)ok;
+}
+
+}  // namespace
+
+// Split count of the tensor-core decode path: about two CTAs per SM.
+int decode_mma_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t range) {
+  const int64_t G = Hq / Hkv;
+  const int64_t ctas = B * Hkv * ((G + QR - 1) / QR);
+  int64_t s = (2LL * num_sms() + ctas - 1) / (ctas > 0 ? ctas : 1);
+  int64_t maxs = (range + KT - 1) / KT;
+  if (maxs < 1) maxs = 1;
+  if (s > maxs) s = maxs;
+  if (s > 64) s = 64;
+  return (int)(s < 1 ? 1 : s);
+}
+
+int decode_mma_launch(DecMmaArgs& a, const void* k_cache, const void* v_cache, int64_t c_sb,
+                      int64_t c_sh, int64_t c_ss, int64_t B, int64_t D, int dtype,
+                      cudaStream_t st) {
+  CUtensorMap tk, tv;
+  const uint64_t smax = (uint64_t)(a.max_seqlen > 0 ? a.max_seqlen : 1);
+  const uint64_t dims[4] = {(uint64_t)D, smax, (uint64_t)a.Hkv, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)c_ss * 2, (uint64_t)c_sh * 2, (uint64_t)c_sb * 2};
+  const uint32_t box[4] = {64, KT, 1, 1};
+  int rc = make_tmap(&tk, k_cache, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != TPP_OK) return rc;
+  rc = make_tmap(&tv, v_cache, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != TPP_OK) return rc;
+  a.passes = (a.G + QR - 1) / QR;
+  a.cluster = a.splits <= 8 ? 1 : 0;
+  const dim3 grid((unsigned)a.splits, (unsigned)(a.Hkv * a.passes), (unsigned)B);
+  auto go = [&](auto kern, size_t smem) -> int {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      set_error("decode_mma_kernel: cannot reserve shared memory");
+      return TPP_ERR_LAUNCH;
+    }
+    return launch("decode_mma_kernel", kern, grid, dim3(kThreads), smem, st,
+                  0u, tk, tv, a);
+  };
+  // the cluster spans the split dimension (x); launch() clusters along y, so
+  // build the launch here when needed
+  if (a.cluster && a.splits > 1) {
+    auto launch_x = [&](auto kern, size_t smem) -> int {
+      // (set on every call: one cache per lambda would be shared by the
+      // fp16 and bf16 kernels, whose pointers have the same type)
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess) {
+        set_error("decode_mma_kernel: cannot reserve shared memory");
+        return TPP_ERR_LAUNCH;
+      }
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      unsigned na = 0;
+      if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+      }
+      attr[na].id = cudaLaunchAttributeClusterDimension;
+      attr[na].val.clusterDim.x = (unsigned)a.splits;
+      attr[na].val.clusterDim.y = 1;
+      attr[na].val.clusterDim.z = 1;
+      ++na;
+      cfg.attrs = attr;
+      cfg.numAttrs = na;
+      const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tk, tv, a);
+      if (e != cudaSuccess) {
+        set_error(std::string("decode_mma_kernel: ") + cudaGetErrorString(e));
+        return TPP_ERR_LAUNCH;
+      }
+      return check_launch("decode_mma_kernel");
+    };
+    return TPP_DISPATCH_HALF(dtype, T, [&] {
+      return D == 64 ? launch_x(decode_mma_kernel<T, 64>, DecSmem<64>::kBytes)
+                     : launch_x(decode_mma_kernel<T, 128>, DecSmem<128>::kBytes);
+    });
+  }
+  return TPP_DISPATCH_HALF(dtype, T, [&] {
+    return D == 64 ? go(decode_mma_kernel<T, 64>, DecSmem<64>::kBytes)
+                   : go(decode_mma_kernel<T, 128>, DecSmem<128>::kBytes);
+  });
+}
+
+}  // namespace tpp
