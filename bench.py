@@ -171,20 +171,23 @@ def linear_roofline(eng, reps: int = 20) -> dict:
     byts = 0
     calls = []
     for L in eng.layers:
-        calls += [(eng.h, L["wqkv"], "none", None, eng.qkv.view(B, -1)),
-                  (eng.o.view(B, -1), L["wo"], "none", eng.x, eng.x),
-                  (eng.h, L["wgu"], "swiglu", None, eng.ff),
-                  (eng.ff, L["wdown"], "none", eng.x, eng.x)]
-    calls.append((eng.h, eng.lm_head, "none", None, eng.logits))
-    for x, w, act, r, y in calls:
+        calls += [(eng.x, L["wqkv_f"], "none", None, eng.qkv.view(B, -1), True),
+                  (eng.o.view(B, -1), L["wo"], "none", eng.x, eng.x, False),
+                  (eng.x, L["wgu_f"], "swiglu", None, eng.ff, True),
+                  (eng.ff, L["wdown"], "none", eng.x, eng.x, False)]
+    calls.append((eng.x, eng.lm_head_f, "none", None, eng.logits, True))
+    for x, w, act, r, y, nrm in calls:
         byts += w.numel() * 2 + x.numel() * 2 + y.numel() * 2 * (2 if r is not None else 1)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
         with torch.cuda.graph(g, stream=s):
-            for x, w, act, r, y in calls:
-                ops.linear(x, w, act=act, residual=r, out=y)
+            for x, w, act, r, y, nrm in calls:
+                if nrm:
+                    ops.rmsnorm_linear(x, w, 1e-6, act=act, out=y)
+                else:
+                    ops.linear(x, w, act=act, residual=r, out=y)
     torch.cuda.current_stream().wait_stream(s)
     for _ in range(3):
         g.replay()
@@ -265,7 +268,7 @@ def run_ours(args, rank, world, local):
     rl = linear_roofline(eng)
     peak, peak_kind = peaks()
     achieved = rl["bytes_per_launch"] / rl["avg_launch_s"] / 1e9
-    roofline = {"kernel": "linear_decode_kernel (all decode-step linears incl. LM head)",
+    roofline = {"kernel": "linear_skinny_kernel (all decode-step linears incl. LM head)",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind}",
                 "traffic": None, "bytes_per_launch": rl["bytes_per_launch"],

@@ -120,6 +120,19 @@ int tpp_linear(const void* x, int64_t ldx, const void* w, const void* bias,
                const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
                int64_t K, int act, int dtype, void* stream);
 
+/* Decode-step fusion of RMSNorm into the following linear (M <= 64 rows):
+ *   y = act( rsqrt(mean(x[m,:]^2) + eps) * (x[m,:] . w_folded^T) + bias ) + residual
+ * where the caller has folded the norm weight into the matrix once,
+ * w_folded[n,k] = w[n,k] * gamma[k]; activations/bias/residual/SwiGLU as in
+ * tpp_linear.  The statistics come from the x tiles the GEMM already stages,
+ * so the separate norm kernel (and its round trip through HBM) disappears.
+ * Replaces the rms_norm1/rms_norm2 -> projection pairs of
+ * examples/LLM/fastqwen3.py:108-115 (RmsNormFused, torchpp/dlops/
+ * normalization.py:30-50, followed by nn.Linear / LinearSILU). */
+int tpp_rmsnorm_linear(const void* x, int64_t ldx, const void* w_folded, const void* bias,
+                       const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
+                       int64_t K, float eps, int act, int dtype, void* stream);
+
 /* y[N] = W[N,K] . x[K]   (fp32 accumulation; y in dtype)
  * Replaces launchHgemv / launchHgemvCute (hgemv_kernels.cuh:69-85, 240-262),
  * which accumulated in fp16. */

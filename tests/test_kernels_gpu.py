@@ -167,6 +167,24 @@ def test_linear_tensor_core_bias_residual():
     _linear_case(200, 3072, 1024, "swiglu", torch.float16, bias=True, residual=True)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("act", ["none", "swiglu", "silu"])
+@pytest.mark.parametrize("MNK", [(32, 4096, 1024), (1, 1024, 1024), (64, 151936, 1024),
+                                 (7, 1000, 200), (17, 3072, 1024)])
+def test_rmsnorm_linear_fused(dtype, act, MNK):
+    M, N, K = MNK
+    g = gen(17)
+    x = rnd(M, K, g=g, dtype=dtype)
+    gamma = rnd(K, g=g, mean=1.0, std=0.1, dtype=dtype)
+    rows = 2 * N if act == "swiglu" else N
+    w = rnd(rows, K, g=g, std=0.02, dtype=dtype)
+    r = rnd(M, N, g=g, dtype=dtype)
+    wf = ops.fold_rmsnorm_weight(w.to(DEV), gamma.to(DEV))
+    y = ops.rmsnorm_linear(x.to(DEV), wf, 1e-6, act=act, residual=r.to(DEV))
+    h = O.rmsnorm(x, gamma, 1e-6)
+    check(y, O.linear(h, w, None, act, r))
+
+
 @pytest.mark.parametrize("KN", [(1024, 2048), (1024, 3072), (3072, 1024), (1024, 151936)])
 def test_hgemv_sweep(KN):
     K, N = KN
@@ -228,6 +246,7 @@ def test_attention_prefill_reads_bhsd_cache_views():
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("case", [
     (4, 16, 8, 128, [1, 100, 1000, 5000], -1),
+    (8, 16, 8, 128, [700, 1, 64, 65, 513, 2000, 129, 300], -1),  # splits merged in a cluster
     (3, 16, 8, 128, [4096, 4097, 9000], 4095),   # sliding window 4096
     (2, 16, 1, 128, [33, 700], -1),               # MQA
     (2, 8, 8, 64, [64, 1], -1),                   # MHA, D=64

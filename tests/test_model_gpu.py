@@ -69,18 +69,23 @@ def test_cached_decode_matches_full_forward():
     assert (inc - full).abs().max().item() < 5e-2 * max(1.0, full.abs().max().item())
 
 
-def test_engine_graph_greedy_matches_eager_generate():
+def test_engine_graph_greedy_is_argmax_of_eager_model():
+    """Every token the CUDA-graph engine picks is an argmax (up to rounding
+    ties) of the eager modules' logits on the engine's own sequence.  (Token-
+    by-token equality with an eager greedy run is not required: the engine
+    folds norm weights into the projections, and on a random model a rounding-
+    level near-tie can flip one token, after which the sequences diverge.)"""
     m = make(torch.bfloat16, seed=3)
     ids = torch.randint(0, 1000, (4, 33), generator=torch.Generator().manual_seed(4))
     with torch.inference_mode():
-        eager = super(Qwen3, m).generate(ids.to(DEV), max_new_token=12,
-                                         sampling_strategy="greedy").cpu()
-        graph = m.generate(ids, max_new_token=12, sampling_strategy="greedy").cpu()
-    assert graph.shape == eager.shape == (4, 45)
-    assert torch.equal(graph[:, :33], ids)
-    # bf16 rounding can flip a near-tie; require near-complete agreement
-    agree = (graph[:, 33:] == eager[:, 33:]).float().mean().item()
-    assert agree >= 0.9, agree
+        out = m.generate(ids, max_new_token=12, sampling_strategy="greedy")
+        assert out.shape == (4, 45)
+        assert torch.equal(out[:, :33].cpu(), ids)
+        logits = m.forward_impl(out[:, :-1].to(DEV)).float()[:, 32:]   # predicts tokens 33..44
+    picked = logits.gather(-1, out[:, 33:].to(DEV)[..., None])[..., 0]
+    best = logits.max(-1).values
+    tol = 5e-2 * best.abs().clamp(min=1.0)
+    assert bool((picked >= best - tol).all()), (best - picked).max().item()
 
 
 def test_engine_step_logits_match_oracle_teacher_forced():

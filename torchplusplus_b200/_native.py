@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_qkrope": (_i32, [_p, _p, _p, _p, _i64, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i32, _p]),
     "tpp_linear": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p]),
+    "tpp_rmsnorm_linear": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _i32,
+                                  _i32, _p]),
     "tpp_hgemv": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
     "tpp_attention_prefill": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64,
                                      _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -6,7 +6,7 @@
 namespace tpp {
 int linear_decode(const void* x, int64_t ldx, const void* w, const void* bias,
                   const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                  int act, int dtype, cudaStream_t st);
+                  int act, int dtype, cudaStream_t st, float norm_eps);
 int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const void* residual,
               void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, int dtype,
               cudaStream_t st);
@@ -30,11 +30,29 @@ extern "C" int tpp_linear(const void* x, int64_t ldx, const void* w, const void*
   if (M == 0) return TPP_OK;
   cudaStream_t st = as_stream(stream);
   if (M <= kDecodeMaxM)
-    return linear_decode(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st);
+    return linear_decode(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st, -1.f);
   return linear_tc(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st);
 }
 
 extern "C" int tpp_hgemv(const void* W, const void* x, void* y, int64_t N, int64_t K, int dtype,
                          void* stream) {
   return tpp_linear(x, K, W, nullptr, nullptr, y, N, 1, N, K, TPP_ACT_NONE, dtype, stream);
+}
+
+extern "C" int tpp_rmsnorm_linear(const void* x, int64_t ldx, const void* w_folded,
+                                  const void* bias, const void* residual, void* y, int64_t ldy,
+                                  int64_t M, int64_t N, int64_t K, float eps, int act, int dtype,
+                                  void* stream) {
+  if (M == 0) return TPP_OK;
+  TPP_REQUIRE(x && w_folded && y, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(M > 0 && N > 0 && K > 0 && N <= 0x3fffffff && K <= 0x7fffffff, TPP_ERR_SHAPE,
+              "bad sizes");
+  TPP_REQUIRE(M <= kDecodeMaxM, TPP_ERR_UNSUPPORTED,
+              "the fused norm+linear serves decode shapes (M <= 64); use tpp_rmsnorm + tpp_linear");
+  TPP_REQUIRE(ldx >= K && ldy >= N && eps >= 0.f, TPP_ERR_SHAPE, "bad strides or eps");
+  TPP_REQUIRE(act >= TPP_ACT_NONE && act <= TPP_ACT_SWIGLU, TPP_ERR_UNSUPPORTED, "unknown activation");
+  TPP_REQUIRE(K % 8 == 0 && ldx % 8 == 0 && aligned16(x) && aligned16(w_folded), TPP_ERR_ALIGN,
+              "x and W rows must be 16-byte aligned (K and ldx multiples of 8)");
+  return linear_decode(x, ldx, w_folded, bias, residual, y, ldy, M, N, K, act, dtype,
+                       as_stream(stream), eps);
 }

@@ -47,7 +47,7 @@ template <int BN>
 constexpr uint32_t stage_b() { return BN * BK * 2; }
 template <int BN>
 constexpr size_t smem_bytes() {
-  return (size_t)kStages * (kStageA + stage_b<BN>()) + 1024 + 256;
+  return (size_t)kStages * (kStageA + stage_b<BN>()) + 1024 + 256 + 4096;
 }
 
 struct SkinnyArgs {
@@ -59,6 +59,7 @@ struct SkinnyArgs {
   int act;
   int kb_per_split;
   int vec_ok;
+  float eps;  // fused RMSNorm of x (NORM variant)
   int* err;
 };
 
@@ -85,7 +86,7 @@ __device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float* v) {
   }
 }
 
-template <typename T, int BN, bool SWIGLU>
+template <typename T, int BN, bool SWIGLU, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_skinny_kernel(const __grid_constant__ CUtensorMap tm_w,
                          const __grid_constant__ CUtensorMap tm_x, SkinnyArgs p) {
@@ -103,6 +104,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* accum = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  // RMSNorm statistics (fused-norm variant): own partial sum of squares per
+  // token, the partials received from every cluster rank, final 1/rms.
+  float* ss_part = reinterpret_cast<float*>(smem + kStages * (kStageA + kStageB) + 128);
+  float* ss_recv = ss_part + 64;   // [8][64]
+  float* rtok = ss_recv + 8 * 64;  // [64]
   // Reused once every MMA has completed: the split-K receive buffer (128 rows
   // in total over all source ranks) and the rank's staged output slice.
   float* recv = reinterpret_cast<float*>(smem);            // [csize][rows][RS]
@@ -131,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_x);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], NORM ? 3 : 1);  // MMA commit (+ the two norm warps)
     }
     mbar_init(accum, 1);
     fence_mbar_init();
@@ -192,6 +198,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_commit(accum);
   } else {
     pdl_wait();
+    if (NORM && warp >= 2) {
+      // ---------------- RMSNorm statistics from the staged x tiles ----------------
+      constexpr int TPR = 64 / BN;   // threads per token row
+      constexpr int CPT = 8 / TPR;   // 16-byte chunks per thread (a row is 128 B)
+      const int tid2 = threadIdx.x - 64;
+      const int t = tid2 / TPR, part = tid2 % TPR;
+      float ss = 0.f;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % kStages;
+        ok = mbar_wait(&full[s], (i / kStages) & 1, p.err, 14);
+        if (!ok) break;
+        const uint8_t* xr = sB + s * kStageB + t * 128 + part * CPT * 16;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) {
+          float f[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(xr + q * 16), f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+#pragma unroll
+      for (int o = TPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (part == 0) ss_part[t] = ss;
+    }
   }
   __syncwarp();
 
@@ -215,6 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < BN; ++j) v[j] = 0.f;
   }
   TPP_TS(3);
+  if (NORM) {
+    __syncthreads();  // ss_part complete
+    if (csize == 1 && threadIdx.x < BN)
+      rtok[threadIdx.x] = rsqrtf(ss_part[threadIdx.x] / (float)p.K + p.eps);
+    if (csize == 1) __syncthreads();
+  }
   if (csize > 1) {
     // The receive buffer aliases every rank's TMA ring: a rank may only be
     // written to once its own MMAs are done, so arrive here and wait below.
@@ -229,6 +267,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t rdst;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"(owner));
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (NORM && threadIdx.x < BN) {
+      // every rank needs every rank's sum of squares for token threadIdx.x
+      const uint32_t sdst = smem_u32(ss_recv + crank * 64 + threadIdx.x);
+      for (int r = 0; r < csize; ++r) {
+        uint32_t rs;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rs) : "r"(sdst), "r"(r));
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(rs), "f"(ss_part[threadIdx.x])
+                     : "memory");
+      }
+    }
 #pragma unroll
     for (int j = 0; j < BN; j += 4)
       asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + 4 * j),
@@ -236,6 +284,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                    : "memory");
     cluster.sync();
     TPP_TS(4);
+    if (NORM) {
+      if (threadIdx.x < BN) {
+        float ss = 0.f;
+        for (int r = 0; r < csize; ++r) ss += ss_recv[r * 64 + threadIdx.x];
+        rtok[threadIdx.x] = rsqrtf(ss / (float)p.K + p.eps);
+      }
+      __syncthreads();
+    }
     // token-fastest mapping: conflict-free reads of recv rows and (per + 1 is
     // odd) conflict-free writes of stage columns
     for (int e = threadIdx.x; e < per * BN; e += kThreads) {
@@ -245,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         g += recv[(r * rows_per + ol) * RSV + t];
         if (SWIGLU) u += recv[(r * rows_per + per + ol) * RSV + t];
       }
+      if (NORM) { g *= rtok[t]; u *= rtok[t]; }
       const int n = out0 + o0 + ol;
       float out = 0.f;
       if (n < p.N) {
@@ -260,6 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     TPP_TS(4);
+    if (NORM) {
+#pragma unroll
+      for (int j = 0; j < BN; ++j) v[j] *= rtok[j];
+    }
     if (SWIGLU) {
       // up rows (warps 2, 3) hand their values to the gate rows via smem
       if (row >= BM / 2) {
@@ -331,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, TCOLS);
 }
 
-template <typename T, int BN, bool SW>
+template <typename T, int BN, bool SW, bool NORM>
 int launch_skinny(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int dtype,
                   cudaStream_t st) {
   constexpr int NOUT = SW ? BM / 2 : BM;
@@ -361,7 +422,7 @@ int launch_skinny(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int 
   // reduce-scatter); a split may end up with fewer k-blocks than others
   ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
   a.kb_per_split = (nkb + ks - 1) / ks;
-  auto kern = linear_skinny_kernel<T, BN, SW>;
+  auto kern = linear_skinny_kernel<T, BN, SW, NORM>;
   constexpr size_t smem = smem_bytes<BN>();
   static unsigned long long configured = 0;  // one bit per device
   int dev = 0;
@@ -379,18 +440,18 @@ int launch_skinny(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int 
                 dim3(kThreads), smem, st, (unsigned)ks, tw, tx, a);
 }
 
-template <typename T>
+template <typename T, bool NORM>
 int skinny_dispatch(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int dtype,
                     cudaStream_t st) {
   const bool sw = a.act == TPP_ACT_SWIGLU;
   if (a.M <= 16)
-    return sw ? launch_skinny<T, 16, true>(x, ldx, w, a, dtype, st)
-              : launch_skinny<T, 16, false>(x, ldx, w, a, dtype, st);
+    return sw ? launch_skinny<T, 16, true, NORM>(x, ldx, w, a, dtype, st)
+              : launch_skinny<T, 16, false, NORM>(x, ldx, w, a, dtype, st);
   if (a.M <= 32)
-    return sw ? launch_skinny<T, 32, true>(x, ldx, w, a, dtype, st)
-              : launch_skinny<T, 32, false>(x, ldx, w, a, dtype, st);
-  return sw ? launch_skinny<T, 64, true>(x, ldx, w, a, dtype, st)
-            : launch_skinny<T, 64, false>(x, ldx, w, a, dtype, st);
+    return sw ? launch_skinny<T, 32, true, NORM>(x, ldx, w, a, dtype, st)
+              : launch_skinny<T, 32, false, NORM>(x, ldx, w, a, dtype, st);
+  return sw ? launch_skinny<T, 64, true, NORM>(x, ldx, w, a, dtype, st)
+            : launch_skinny<T, 64, false, NORM>(x, ldx, w, a, dtype, st);
 }
 
 }  // namespace
@@ -402,15 +463,21 @@ extern "C" void tpp_debug_stamps(unsigned long long* host, int n) {
 #endif
 
 // Entry used by tpp_linear (linear.cu) for M <= 64.
+// norm_eps >= 0: x is RMS-normalised on the fly (the caller has folded the
+// norm weight into W); norm_eps < 0: plain linear.
 int linear_decode(const void* x, int64_t ldx, const void* w, const void* bias,
                   const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                  int act, int dtype, cudaStream_t st) {
+                  int act, int dtype, cudaStream_t st, float norm_eps) {
   SkinnyArgs a;
   a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
   a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act; a.kb_per_split = 0;
   a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned16(y) && (!residual || aligned16(residual));
   a.err = device_error_flag();
-  return TPP_DISPATCH_HALF(dtype, T, [&] { return skinny_dispatch<T>(x, ldx, w, a, dtype, st); });
+  a.eps = norm_eps;
+  return TPP_DISPATCH_HALF(dtype, T, [&] {
+    return norm_eps >= 0.f ? skinny_dispatch<T, true>(x, ldx, w, a, dtype, st)
+                           : skinny_dispatch<T, false>(x, ldx, w, a, dtype, st);
+  });
 }
 
 }  // namespace tpp

@@ -2,12 +2,13 @@
 CUDA graph of sm_100a kernels, with every buffer static and the sampled token
 fed back on the device.
 
-Per step and layer: rmsnorm -> QKV linear -> fused q/k-norm + RoPE + KV write
--> split-KV decode attention (+ merge) -> o-proj linear with the residual add
-in its epilogue -> rmsnorm -> gate/up linear with the SwiGLU product in its
-epilogue -> down linear with the residual add in its epilogue.  Then final
-rmsnorm -> LM-head linear -> argmax -> decode_advance (token history,
-positions).  Nothing returns to the host between steps.
+Per step and layer (6 kernels): RMSNorm+QKV linear (norm fused into the
+GEMM) -> fused q/k-norm + RoPE + KV write -> tensor-core decode attention
+(split-KV merged in a cluster) -> o-proj linear with the residual add in its
+epilogue -> RMSNorm+gate/up linear with the SwiGLU product in its epilogue ->
+down linear with the residual add in its epilogue.  Then RMSNorm+LM-head
+linear -> argmax -> decode_advance (token history, positions).  Nothing
+returns to the host between steps.
 
 This replaces the reference's per-token Python loop (torchpp/llmops/llm.py:
 263-282), which issues ~20 launches per layer from Python, copies the whole
@@ -39,18 +40,26 @@ class DecodeEngine:
         self.Hq, self.Hkv, self.D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         self.eps = 1e-6
         self.layers = []
+        # The decode step runs each RMSNorm inside the following projection
+        # (tpp_rmsnorm_linear), with the norm weight folded into that
+        # projection's matrix once here.  These folded copies belong to the
+        # engine; rebuild the engine after changing the model's weights.
         for blk in model.transformer_blocs:
             a = blk.attn
+            n1, n2 = blk.rms_norm1.weight.detach(), blk.rms_norm2.weight.detach()
             self.layers.append(dict(
-                n1=blk.rms_norm1.weight.detach(), n2=blk.rms_norm2.weight.detach(),
+                n1=n1, n2=n2,
                 wqkv=a._qkv.get(a.Wq.weight, a.Wk.weight, a.Wv.weight),
+                wqkv_f=ops.fold_rmsnorm_weight(a._qkv.get(a.Wq.weight, a.Wk.weight, a.Wv.weight), n1),
                 qn=a.q_norm.weight.detach() if a.q_norm is not None else None,
                 kn=a.k_norm.weight.detach() if a.k_norm is not None else None,
                 wo=a.out_projection.weight.detach(),
                 wgu=blk.ffn.gate_up_weight(),
+                wgu_f=ops.fold_rmsnorm_weight(blk.ffn.gate_up_weight(), n2),
                 wdown=blk.ffn.linear_layer2.weight.detach()))
         self.nf = model.final_rmsnorm.weight.detach()
         self.lm_head = model.out_head.weight.detach()
+        self.lm_head_f = ops.fold_rmsnorm_weight(self.lm_head, self.nf)
         self.emb = model.tok_embed.weight.detach()
         self.cos, self.sin = model.cos, model.sin
         if self.cos.shape[0] < max_seq_len:
@@ -83,18 +92,15 @@ class DecodeEngine:
         B, Hq, Hkv, D = self.batch_size, self.Hq, self.Hkv, self.D
         ops.embedding(self.tokens, self.emb, out=self.x)
         for L, c in zip(self.layers, self.caches):
-            ops.rmsnorm(self.x, L["n1"], self.eps, out=self.h)
-            ops.linear(self.h, L["wqkv"], out=self.qkv.view(B, -1))
+            ops.rmsnorm_linear(self.x, L["wqkv_f"], self.eps, out=self.qkv.view(B, -1))
             ops.qk_norm_rope_cache(self.qkv, L["qn"], L["kn"], self.eps, self.cos, self.sin,
                                    self.positions, c.k_cache, c.v_cache, Hq, Hkv, q_out=self.q)
             ops.attention_decode(self.q.view(B, Hq, D), c.k_cache, c.v_cache, self.seqlens,
                                  self.max_seq_len, out=self.o, workspace=self.ws)
             ops.linear(self.o.view(B, Hq * D), L["wo"], residual=self.x, out=self.x)
-            ops.rmsnorm(self.x, L["n2"], self.eps, out=self.h)
-            ops.linear(self.h, L["wgu"], act="swiglu", out=self.ff)
+            ops.rmsnorm_linear(self.x, L["wgu_f"], self.eps, act="swiglu", out=self.ff)
             ops.linear(self.ff, L["wdown"], residual=self.x, out=self.x)
-        ops.rmsnorm(self.x, self.nf, self.eps, out=self.h)
-        ops.linear(self.h, self.lm_head, out=self.logits)
+        ops.rmsnorm_linear(self.x, self.lm_head_f, self.eps, out=self.logits)
         ops.argmax(self.logits, out=self.tokens)
         ops.decode_advance(self.tokens, self.out_ids, self.positions, self.seqlens)
 

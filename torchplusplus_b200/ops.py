@@ -185,6 +185,38 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     return out
 
 
+def fold_rmsnorm_weight(weight: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
+    """W' = W * gamma[None, :] (rounded once to W's dtype): the matrix
+    rmsnorm_linear expects.  One-time preparation, not a hot-path op."""
+    return (weight.float() * gamma.float()[None, :]).to(weight.dtype).contiguous()
+
+
+def rmsnorm_linear(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-6,
+                   bias: torch.Tensor | None = None, act: str = "none",
+                   residual: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """linear(rmsnorm(x, gamma), W) for decode shapes (<= 64 rows) in one
+    kernel; `w_folded` = fold_rmsnorm_weight(W, gamma)."""
+    _cuda(x, w_folded, bias, residual, out)
+    dt = _half(x, "x")
+    _same_dtype(x, w_folded, bias, residual)
+    K = x.shape[-1]
+    code = N.ACT_CODE[act]
+    Nout = w_folded.shape[0] // 2 if act == "swiglu" else w_folded.shape[0]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or (x2.shape[0] > 1 and x2.stride(0) % 8):
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty((*x.shape[:-1], Nout), dtype=x.dtype, device=x.device)
+    y2 = out.view(-1, Nout)
+    r2 = residual.contiguous().view(-1, Nout) if residual is not None else None
+    N.call("tpp_rmsnorm_linear", x2.data_ptr(), x2.stride(0) if M > 1 else K,
+           w_folded.data_ptr(), N.ptr(bias), N.ptr(r2), y2.data_ptr(), Nout, M, Nout, K,
+           float(eps), code, dt, N.stream_of(x))
+    return out
+
+
 def hgemv(weight: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """y[N] = weight[N,K] @ x[K] with fp32 accumulation."""
     _cuda(weight, x)
