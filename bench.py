@@ -203,6 +203,124 @@ def linear_roofline(eng, reps: int = 20) -> dict:
             "bytes_per_launch": byts / len(calls), "avg_launch_s": t / len(calls)}
 
 
+def _time_graph(fn_list, reps: int = 5) -> float:
+    """Captures the callables (one launch sequence) in a CUDA graph, replays it
+    `reps` times and returns seconds per replay (CUDA events)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fn_list:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for f in fn_list:
+                f()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+def per_op(hbm_peak: float, tc_peak: float) -> dict:
+    """Per-op achieved throughput on the BASELINE configs 1, 2, 3 and 5.
+
+    Each op is launched over enough distinct input copies that the bytes
+    touched per replay exceed L2 (126 MB), so every launch streams from HBM;
+    the time per launch is the graph replay time / launches."""
+    from torchplusplus_b200 import ops
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    res = {}
+
+    def rnd(*shape, dtype=torch.float16, std=1.0, mean=0.0):
+        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std + mean).to(dtype)
+
+    def copies(nbytes):
+        return max(1, min(64, int(2 * 126e6 // max(nbytes, 1)) + 1))
+
+    def rec(name, t, work, unit):
+        if unit == "GB/s":
+            ach = work / t / 1e9
+            res[name] = {"us": t * 1e6, "achieved": ach, "unit": unit, "frac_hbm": ach / hbm_peak}
+        else:
+            ach = work / t / 1e12
+            res[name] = {"us": t * 1e6, "achieved": ach, "unit": unit, "frac_tc": ach / tc_peak}
+
+    # config 1: RMSNorm [2048, 1024] fp16, then Linear+SiLU 2048x3072x1024
+    nb = 2 * 2 * 2048 * 1024 + 2 * 1024
+    n = copies(nb)
+    xs = [rnd(2048, 1024) for _ in range(n)]
+    ys = [torch.empty_like(xs[0]) for _ in range(n)]
+    w = rnd(1024, mean=1.0, std=0.1)
+    t = _time_graph([lambda i=i: ops.rmsnorm(xs[i], w, 1e-6, out=ys[i]) for i in range(n)]) / n
+    rec("cfg1_rmsnorm_2048x1024_f16", t, nb, "GB/s")
+    W = rnd(3072, 1024, std=0.02)
+    yl = torch.empty(2048, 3072, device=dev, dtype=torch.float16)
+    t = _time_graph([lambda: ops.linear(xs[0], W, act="silu", out=yl)] * 10) / 10
+    rec("cfg1_linear_silu_2048x3072x1024_f16", t, 2 * 2048 * 3072 * 1024, "TFLOP/s")
+    del xs, ys
+
+    # config 2: RoPE on Q [4,16,2048,128] + K [4,8,2048,128]; causal GQA prefill
+    q = rnd(4, 16, 2048, 128)
+    k = rnd(4, 8, 2048, 128)
+    cos, sin = (torch.cos(torch.arange(2048 * 128, device=dev).view(2048, 128) * 1e-3).half(),
+                torch.sin(torch.arange(2048 * 128, device=dev).view(2048, 128) * 1e-3).half())
+    nb = 2 * 2 * (q.numel() + k.numel())
+    t = _time_graph([lambda: ops.qkrope(q, k, cos, sin)] * 5) / 5
+    rec("cfg2_qkrope_B4_S2048_Hq16_Hk8_D128_f16", t, nb, "GB/s")
+    qa = rnd(4, 2048, 16, 128)
+    ka = rnd(4, 2048, 8, 128)
+    va = rnd(4, 2048, 8, 128)
+    oa = torch.empty_like(qa)
+    t = _time_graph([lambda: ops.attention(qa, ka, va, causal=True, out=oa)] * 5) / 5
+    rec("cfg2_attention_causal_gqa_B4_S2048_f16", t, 4 * 4 * 16 * 2048 * 2048 * 128 / 2, "TFLOP/s")
+    del q, k, qa, ka, va, oa
+
+    # config 3: decode GEMV sweep (batch 1) and fused Linear+SiLU at M = 1, 32
+    for K_, N_ in ((1024, 2048), (1024, 3072), (3072, 1024), (1024, 151936)):
+        nb = 2 * (N_ * K_ + K_ + N_)
+        n = copies(nb)
+        Ws = [rnd(N_, K_, std=0.02) for _ in range(n)]
+        x1 = rnd(K_)
+        t = _time_graph([lambda i=i: ops.hgemv(Ws[i], x1) for i in range(n)]) / n
+        rec(f"cfg3_hgemv_K{K_}_N{N_}_f16", t, nb, "GB/s")
+        del Ws
+    for M_ in (1, 32):
+        nb = 2 * (3072 * 1024 + M_ * 1024 + M_ * 3072)
+        n = copies(nb)
+        Ws = [rnd(3072, 1024, std=0.02) for _ in range(n)]
+        xm = rnd(M_, 1024)
+        t = _time_graph([lambda i=i: ops.linear(xm, Ws[i], act="silu") for i in range(n)]) / n
+        rec(f"cfg3_linear_silu_M{M_}_K1024_N3072_f16", t, nb, "GB/s")
+        del Ws
+
+    # config 5: sliding-window GQA decode, B64, Hq16/Hkv8, D128, window 4096, bf16
+    for L in (1024, 4096, 16384, 32768):
+        B = 64
+        kc = rnd(B, 8, L, 128, dtype=torch.bfloat16)
+        vc = rnd(B, 8, L, 128, dtype=torch.bfloat16)
+        qd = rnd(B, 16, 128, dtype=torch.bfloat16)
+        od = torch.empty_like(qd)
+        sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+        ws = torch.empty(max(16, ops.decode_workspace_bytes(B, 16, L, 128)), dtype=torch.uint8,
+                         device=dev)
+        nb = B * (2 * min(L, 4096) * 8 * 128 * 2 + 2 * 16 * 128 * 2)
+        t = _time_graph([lambda: ops.attention_decode(qd, kc, vc, sl, L, window_left=4095,
+                                                      out=od, workspace=ws)] * 10) / 10
+        rec(f"cfg5_swa_decode_B64_L{L}_w4096_bf16", t, nb, "GB/s")
+        del kc, vc
+    torch.cuda.synchronize()
+    return res
+
+
 def run_ours(args, rank, world, local):
     from torchplusplus_b200 import _native as N
     from torchplusplus_b200.llmops.qwen3 import Qwen3, Qwen3Config
@@ -289,6 +407,16 @@ def run_ours(args, rank, world, local):
         extra["batch1_decode_tokens_per_s"] = nrep / (a0.elapsed_time(a1) / 1e3)
         model._engine = None
 
+    lps = eng.launches_per_step or 0
+    ops_res = None
+    if rank == 0 and not args.skip_ops:
+        model._engine = None
+        del eng
+        torch.cuda.empty_cache()
+        import json as _j
+        peaks_d = _j.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else {"bf16_tflops": 1590.0}
+        ops_res = per_op(peak, float(peaks_d.get("bf16_tflops", 1590.0)))
     if rank != 0:
         return
     cpu = cpu_decode_rate(B, args.cpu_steps, PROMPT) if world == 1 and not args.skip_cpu else None
@@ -304,9 +432,9 @@ def run_ours(args, rank, world, local):
                        "parallelism": f"replicas x{world} (batch-sharded, no collective)",
                        "l2": "inputs larger than L2 (1.19 GB weights + KV per step)"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
-            "gpu_launches": (eng.launches_per_step or 0) * nrep * args.steps,
-            "launches_per_decode_step": eng.launches_per_step,
-            "tpp_launches_total": N.launch_count(), **extra}
+            "gpu_launches": lps * nrep * args.steps,
+            "launches_per_decode_step": lps,
+            "tpp_launches_total": N.launch_count(), "per_op": ops_res, **extra}
     print(json.dumps(line), flush=True)
 
 
@@ -321,6 +449,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=4)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-b1", action="store_true")
+    ap.add_argument("--skip-ops", action="store_true", help="skip the per-op roofline table")
     ap.add_argument("--gen", type=int, default=GEN,
                     help="tokens generated per request (profiling runs use fewer)")
     args = ap.parse_args()
