@@ -106,7 +106,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Activations, fp32 in/out, following csrc/activation/activation.cuh:26-67
 // of the reference (GeLU-tanh with sqrt(2/pi) and 0.044715; SiLU x/(1+e^-x)).
-__device__ __forceinline__ float act_silu(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float act_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float act_gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;

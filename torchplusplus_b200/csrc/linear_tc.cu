@@ -30,7 +30,7 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;  // 128 bytes of fp16/bf16: one swizzle row
 constexpr int kStages = 4;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr uint32_t kStageA = BM * BK * 2;  // 16 KB
 constexpr uint32_t kStageB = BN * BK * 2;  // 32 KB
 constexpr size_t kSmem = (size_t)kStages * (kStageA + kStageB) + 1024 /*align*/ + 256 /*bars*/;
@@ -46,10 +46,22 @@ struct TcArgs {
   int* err;
 };
 
+#ifdef TPP_DEBUG_STAMPS
+__device__ unsigned long long g_tc_stamps[8 * 1024];
+#define TC_TS(i) do { asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st_[i])); } while (0)
+#else
+#define TC_TS(i) do {} while (0)
+#endif
+
 template <typename T, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
-                     const __grid_constant__ CUtensorMap tm_w, TcArgs p) {
+                     const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_y, TcArgs p) {
+#ifdef TPP_DEBUG_STAMPS
+  unsigned long long st_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#endif
+  TC_TS(0);
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: the 128B-swizzle pattern repeats every 8 rows of 128 B.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -69,6 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_y);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -111,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ph = (kb / kStages) & 1;
       ok = mbar_wait(&full[s], ph, p.err, 2);
       if (!ok) break;
+      if (kb == 0) TC_TS(1);
       tc_fence_after();
       const uint32_t a0 = smem_u32(sA + s * kStageA);
       const uint32_t b0 = smem_u32(sB + s * kStageB);
@@ -125,26 +139,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&empty[s]);
     }
     tc_commit(accum);
+    TC_TS(2);
   }
   __syncwarp();
 
-  // ---------------- epilogue (all 4 warps) ----------------
+  // ---------------- epilogue (all 8 warps) ----------------
+  // Warp w reads TMEM lanes 32*(w%4).. (tile rows) and one half of the
+  // output columns; results (bias, activation, SwiGLU, residual applied in
+  // fp32) are staged in shared memory as 128-byte-swizzled [128 x 64] boxes
+  // and written by TMA bulk tensor stores (full-line, coalesced writes).
   const bool got = mbar_wait(accum, 0, p.err, 3);
   tc_fence_after();
-  const int row = m0 + warp * 32 + lane;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  TC_TS(3);
+  constexpr int NOUT = SWIGLU ? BN / 2 : BN;
+  constexpr int HALF = NOUT / 2;  // columns per warp half
+  const int quarter = warp & 3, hc = warp >> 2;
+  const int rl = quarter * 32 + lane;  // tile row
+  const int row = m0 + rl;
+  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
   const T* bias = static_cast<const T*>(p.bias);
   const T* res = static_cast<const T*>(p.residual);
   T* Y = static_cast<T*>(p.y);
-  const bool vec_ok = p.vec_ok != 0;
-  constexpr int NOUT = SWIGLU ? BN / 2 : BN;
+  const bool use_tma = p.vec_ok != 0;
+  uint8_t* sout = smem;  // the operand ring is idle now: NOUT/64 boxes of 16 KB
 #pragma unroll 1
-  for (int c = 0; c < NOUT; c += 32) {
+  for (int cc = 0; cc < HALF; cc += 32) {
+    const int c = hc * HALF + cc;  // first column of this chunk within the tile
     uint32_t r[32], r2[32];
     tmem_ld32(trow + c, r);
     if (SWIGLU) tmem_ld32(trow + BN / 2 + c, r2);
     tmem_wait_ld();
-    if (!got || row >= p.M) continue;
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -161,20 +185,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       v[j] = a;
     }
     const int n0 = n_out0 + c;
-    T* yr = Y + (int64_t)row * p.ldy;
-    const T* rr = res ? res + (int64_t)row * p.ldy : nullptr;
-    if (vec_ok && n0 + 32 <= p.N) {
+    const T* rr = (res && row < p.M) ? res + (int64_t)row * p.ldy : nullptr;
+    if (use_tma) {
+      uint8_t* box = sout + (c >> 6) * (BM * 128);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        if (rr) {
+        if (rr && n0 + q * 8 + 8 <= p.N) {
           float rf[8];
           unpack8<T>(*reinterpret_cast<const uint4*>(rr + n0 + q * 8), rf);
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[q * 8 + j] += rf[j];
+        } else if (rr) {
+          for (int j = 0; j < 8 && n0 + q * 8 + j < p.N; ++j) v[q * 8 + j] += to_f32(rr[n0 + q * 8 + j]);
         }
-        *reinterpret_cast<uint4*>(yr + n0 + q * 8) = pack8<T>(v + q * 8);
+        const int chunk = ((c & 63) >> 3) + q;  // 16-byte chunk within the 128-byte row
+        *reinterpret_cast<uint4*>(box + rl * 128 + ((chunk ^ (rl & 7)) << 4)) =
+            pack8<T>(v + q * 8);
       }
-    } else {
+    } else if (got && row < p.M) {
+      T* yr = Y + (int64_t)row * p.ldy;
       for (int j = 0; j < 32; ++j) {
         const int n = n0 + j;
         if (n >= p.N) break;
@@ -184,12 +213,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (use_tma) {
+    fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA engine
+    __syncthreads();
+    if (threadIdx.x == 0 && got) {
+#pragma unroll
+      for (int b = 0; b < NOUT / 64; ++b) {
+        asm volatile(
+            "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                reinterpret_cast<uint64_t>(&tm_y)),
+            "r"(n_out0 + b * 64), "r"(m0), "r"(smem_u32(sout + b * (BM * 128)))
+            : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
+  }
+  TC_TS(4);
+#ifdef TPP_DEBUG_STAMPS
+  if (threadIdx.x == 32) {  // MMA lane: has 1, 2
+    const int id = blockIdx.y * gridDim.x + blockIdx.x;
+    g_tc_stamps[8 * id + 1] = st_[1]; g_tc_stamps[8 * id + 2] = st_[2];
+  }
+  if (threadIdx.x == 0) {
+    const int id = blockIdx.y * gridDim.x + blockIdx.x;
+    g_tc_stamps[8 * id] = st_[0]; g_tc_stamps[8 * id + 3] = st_[3]; g_tc_stamps[8 * id + 4] = st_[4];
+  }
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, BN);
 }
 
 }  // namespace
+
+#ifdef TPP_DEBUG_STAMPS
+extern "C" void tpp_debug_stamps_tc(unsigned long long* host, int n) {
+  cudaMemcpyFromSymbol(host, g_tc_stamps, sizeof(unsigned long long) * n);
+}
+#endif
 
 int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const void* residual,
               void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, int dtype,
@@ -213,10 +275,21 @@ int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const
     int rc = make_tmap(&tw, w, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != TPP_OK) return rc;
   }
+  CUtensorMap ty;
+  const bool y_tma = (N % 8 == 0) && (ldy % 8 == 0) && aligned16(y);
+  if (y_tma) {
+    uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    uint64_t strides[1] = {(uint64_t)ldy * 2};
+    uint32_t box[2] = {64, BM};
+    int rc = make_tmap(&ty, y, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  } else {
+    ty = tx;  // unused
+  }
   TcArgs a;
   a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
   a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act;
-  a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned16(y) && (!residual || aligned16(residual));
+  a.vec_ok = y_tma && (!residual || aligned16(residual));
   a.err = device_error_flag();
   const int nout = sw ? BN / 2 : BN;
   dim3 grid((unsigned)((N + nout - 1) / nout), (unsigned)((M + BM - 1) / BM), 1);
@@ -227,7 +300,7 @@ int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const
       set_error("linear_tc_kernel: cannot reserve shared memory");
       return (int)TPP_ERR_LAUNCH;
     }
-    return launch("linear_tc_kernel", kern, dim3(grid), dim3(kThreads), kSmem, st, 0, tx, tw, a);
+    return launch("linear_tc_kernel", kern, dim3(grid), dim3(kThreads), kSmem, st, 0, tx, tw, ty, a);
   });
 }
 
