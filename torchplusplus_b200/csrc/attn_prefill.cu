@@ -251,6 +251,13 @@ int prefill_launch(const PrefillArgs& a, int64_t B, cudaStream_t st) {
 }
 
 }  // namespace
+int attn_prefill_tc(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, const void* k,
+                    int64_t k_sb, int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb,
+                    int64_t v_ss, int64_t v_sh, void* o, int64_t o_sb, int64_t o_ss,
+                    int64_t o_sh, int64_t B, int64_t Sq, int64_t Sk, int64_t Hq, int64_t Hkv,
+                    int64_t Dh, int causal, int64_t window_left, float scale, int dtype,
+                    cudaStream_t st);
+
 }  // namespace tpp
 
 using namespace tpp;
@@ -277,6 +284,13 @@ extern "C" int tpp_attention_prefill(const void* q, int64_t q_sb, int64_t q_ss, 
                   (reinterpret_cast<uintptr_t>(o) & 3u) == 0,
               TPP_ERR_ALIGN, "q/k/v must be 16-byte aligned");
   if (B == 0 || Sq == 0) return TPP_OK;
+  cudaStream_t st = as_stream(stream);
+  if (D == 128) {
+    const int rc = attn_prefill_tc(q, q_sb, q_ss, q_sh, k, k_sb, k_ss, k_sh, v, v_sb, v_ss, v_sh,
+                                   o, o_sb, o_ss, o_sh, B, Sq, Sk, Hq, Hkv, D, causal,
+                                   window_left, scale, dtype, st);
+    if (rc != TPP_ERR_UNSUPPORTED) return rc;
+  }
   PrefillArgs a;
   a.q = q; a.q_sb = q_sb; a.q_ss = q_ss; a.q_sh = q_sh;
   a.k = k; a.k_sb = k_sb; a.k_ss = k_ss; a.k_sh = k_sh;
@@ -285,7 +299,6 @@ extern "C" int tpp_attention_prefill(const void* q, int64_t q_sb, int64_t q_ss, 
   a.Sq = (int)Sq; a.Sk = (int)Sk; a.Hq = (int)Hq; a.Hkv = (int)Hkv;
   a.causal = causal; a.window_left = window_left;
   a.scale_log2 = scale * kLog2e;
-  cudaStream_t st = as_stream(stream);
   return TPP_DISPATCH_HALF(dtype, T, [&] {
     return D == 64 ? prefill_launch<T, 64>(a, B, st) : prefill_launch<T, 128>(a, B, st);
   });
