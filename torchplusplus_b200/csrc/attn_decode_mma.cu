@@ -11,7 +11,7 @@
 //  * grid (split, kv_head x head_pass, batch), cluster (splits, 1, 1) when
 //    there are at most 8 splits.  A CTA streams one slice of one kv head's
 //    key range once for all (up to 16) query heads of the group.
-//  * Thread 0 issues 4-D TMA loads (128-byte swizzle, no multicast) of
+//  * Thread 0 issues 4-D TMA loads (128-byte swizzle, per-CTA loads) of
 //    64-key K and V tiles into a kStages ring (full/empty mbarriers, bounded
 //    waits).  Each of the 4 warps takes 16 keys of every tile:
 //    S = Q.K^T (D/16 x 2 MMAs), fp32 online softmax in the exp2 domain,

@@ -8,7 +8,7 @@
 // One CTA = one (batch, query head, 128-query block).  384 threads:
 //   warp 0 / lane 0 : TMA producer: Q once, then K and V tiles of 128 keys
 //                     into separate rings (3 K, 2 V stages; 128-byte swizzle,
-//                     no multicast), K running ahead of V.
+//                     per-CTA loads), K running ahead of V.
 //   warp 1 / lane 0 : MMA issuer:  S_j = Q . K_j^T   (tcgen05, M=N=128, K=128)
 //                                  O  += P_j . V_j   (A = P_j read from TMEM,
 //                                                     B = V_j MN-major in smem)

@@ -6,7 +6,7 @@
 //  * The MMA's M side is 128 weight rows, its N side the (padded) tokens
 //    (BN = 16/32/64): D[128 x BN] += W_tile[128 x 64] . x_tile[BN x 64]^T with
 //    tcgen05.mma kind::f16, fp32 accumulator in TMEM (BN columns).
-//  * W and x tiles arrive by TMA (128-byte swizzle, no multicast) in a
+//  * W and x tiles arrive by TMA (128-byte swizzle, per-CTA loads) in a
 //    kStages-deep shared-memory ring guarded by full/empty mbarriers: up to
 //    kStages x 16 KB of weights in flight per CTA, independent of registers.
 //  * The first kStages weight tiles are requested BEFORE the programmatic-

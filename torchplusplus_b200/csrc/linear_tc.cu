@@ -6,8 +6,8 @@
 // tile).  Two fp32 accumulators live in TMEM so the epilogue of one tile
 // overlaps the MMAs of the next.  384 threads:
 //   warp 0 / lane 0 : TMA producer.  Streams 64-wide K slices of x and W
-//                     through a shared-memory ring (128-byte swizzle, no
-//                     multicast), full/empty mbarrier per stage, continuous
+//                     through a shared-memory ring (128-byte swizzle,
+//                     per-CTA loads), full/empty mbarrier per stage, continuous
 //                     across tiles.
 //   warp 1 / lane 0 : MMA issuer.  tcgen05.mma kind::f16 (M=128, N=BN, K=16)
 //                     x4 per stage into accumulator j%2; tcgen05.commit frees

@@ -1,5 +1,5 @@
 // sm_100a building blocks written directly in PTX: mbarriers with bounded
-// waits, TMA tensor loads (no multicast), tcgen05 MMA / TMEM access, and the
+// waits, TMA tensor loads (per-CTA loads), tcgen05 MMA / TMEM access, and the
 // shared-memory matrix descriptors the tensor core reads operands through.
 #pragma once
 #include <cuda.h>
