@@ -111,12 +111,8 @@ def barrier(world):
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from torchplusplus_b200 import replicas
+    return replicas.max_over_ranks(x, world, "cuda")
 
 
 # ---------------------------------------------------------------- CPU baseline

@@ -133,6 +133,36 @@ int tpp_rmsnorm_linear(const void* x, int64_t ldx, const void* w_folded, const v
                        const void* residual, void* y, int64_t ldy, int64_t M, int64_t N,
                        int64_t K, float eps, int act, int dtype, void* stream);
 
+/* ---- packed decode linears ---------------------------------------------------
+ * A decode step (M <= 64 tokens) is bound by how fast each SM can pull its
+ * operands, and on B200 a CTA's TMA loads of strided 128-byte rows run at
+ * ~25 GB/s while contiguous bulk copies run at >150 GB/s.  The packed forms
+ * below lay the operands out in HBM exactly as the tensor-core kernel stages
+ * them (128-byte-swizzled K-major tiles), so every load is one contiguous copy:
+ *   weights:     per-CTA images, packed once (static);
+ *   activations: [K/64][T][64] with T = 16 or 32 (M <= 32 rounded up),
+ *                written by the previous decode linear as a second output.
+ * Every CTA computes whole outputs (no split-K).  K must be a multiple of 64;
+ * tpp_packed_weight_bytes returns 0 when a layer is too wide for this form
+ * (then use tpp_linear / tpp_rmsnorm_linear).  No reference counterpart: the
+ * reference decodes with nn.Linear / LinearSILU on row-major weights
+ * (examples/LLM/fastqwen3.py:108-115). */
+int64_t tpp_packed_weight_bytes(int64_t N, int64_t K, int act);
+int64_t tpp_packed_activation_bytes(int64_t M, int64_t K);
+/* w [N,K] (or [2N,K] gate rows then up rows for SwiGLU) -> packed image. */
+int tpp_pack_weight(const void* w, int64_t N, int64_t K, int act, int dtype, void* w_packed,
+                    void* stream);
+/* x [M,K] (row stride ldx) -> packed activation. */
+int tpp_pack_activation(const void* x, int64_t ldx, int64_t M, int64_t K, int dtype,
+                        void* x_packed, void* stream);
+/* y = act(scale * (x . W^T) + bias) + residual, x and W packed; scale =
+ * rsqrt(mean(x^2) + eps) when eps >= 0 (fused RMSNorm, norm weight folded
+ * into W as for tpp_rmsnorm_linear), else 1.  y_packed (optional) receives y
+ * in packed form for the next decode linear (needs N % 64 == 0). */
+int tpp_linear_packed(const void* x_packed, const void* w_packed, const void* bias,
+                      const void* residual, void* y, int64_t ldy, void* y_packed, int64_t M,
+                      int64_t N, int64_t K, float eps, int act, int dtype, void* stream);
+
 /* y[N] = W[N,K] . x[K]   (fp32 accumulation; y in dtype)
  * Replaces launchHgemv / launchHgemvCute (hgemv_kernels.cuh:69-85, 240-262),
  * which accumulated in fp16. */

@@ -185,6 +185,47 @@ def test_rmsnorm_linear_fused(dtype, act, MNK):
     check(y, O.linear(h, w, None, act, r))
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", [
+    # (M, N, K, act, fused norm, bias, residual)
+    (32, 4096, 1024, "none", True, False, False),    # Qwen3-0.6B qkv
+    (32, 1024, 2048, "none", False, False, True),    # o-proj + residual
+    (32, 3072, 1024, "swiglu", True, False, False),  # gate/up
+    (32, 1024, 3072, "none", False, False, True),    # down + residual
+    (1, 1000, 512, "silu", False, True, True),       # ragged N, batch 1
+    (20, 640, 192, "gelu", True, True, False),       # BN 32 with 20 tokens
+    (32, 2048, 1024, "swiglu", False, True, True),   # full 32-token tile
+    (9, 9000, 128, "none", False, False, False),     # 64 rows per CTA
+    (3, 4736, 64, "relu", True, False, True),        # one k-block
+])
+def test_linear_packed(dtype, case):
+    M, N, K, act, norm, bias, residual = case
+    g = gen(31)
+    x = rnd(M, K, g=g, dtype=dtype)
+    rows = 2 * N if act == "swiglu" else N
+    w = rnd(rows, K, g=g, std=0.02, dtype=dtype)
+    b = rnd(rows, g=g, std=0.1, dtype=dtype) if bias else None
+    r = rnd(M, N, g=g, dtype=dtype) if residual else None
+    gamma = rnd(K, g=g, mean=1.0, std=0.1, dtype=dtype)
+    wd = w.to(DEV)
+    if norm:
+        wd = ops.fold_rmsnorm_weight(wd, gamma.to(DEV))
+    if not ops.PackedWeight.supported(N, K, act):
+        pytest.skip("layer too wide for the packed form on this device")
+    pw = ops.PackedWeight(wd, act)
+    xp = ops.pack_activation(x.to(DEV))
+    yp = torch.zeros(ops.packed_activation_bytes(M, N), dtype=torch.uint8, device=DEV) \
+        if N % 64 == 0 else None
+    y = ops.linear_packed(xp, M, pw, None if b is None else b.to(DEV),
+                          None if r is None else r.to(DEV), 1e-6 if norm else None,
+                          out_packed=yp)
+    h = O.rmsnorm(x, gamma, 1e-6) if norm else x
+    check(y, O.linear(h, w, b, act, r))
+    if yp is not None:
+        # the packed second output is exactly pack_activation(y)
+        assert torch.equal(yp.cpu(), ops.pack_activation(y).cpu())
+
+
 @pytest.mark.parametrize("KN", [(1024, 2048), (1024, 3072), (3072, 1024), (1024, 151936)])
 def test_hgemv_sweep(KN):
     K, N = KN

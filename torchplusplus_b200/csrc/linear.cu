@@ -10,6 +10,15 @@ int linear_decode(const void* x, int64_t ldx, const void* w, const void* bias,
 int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const void* residual,
               void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, int dtype,
               cudaStream_t st);
+int64_t xs_packed_weight_bytes(int64_t N, int64_t K, int act);
+int64_t xs_packed_activation_bytes(int64_t M, int64_t K);
+int xs_pack_weight(const void* w, int64_t N, int64_t K, int act, void* dst, cudaStream_t st);
+int xs_pack_activation(const void* x, int64_t ldx, int64_t M, int64_t K, void* dst,
+                       cudaStream_t st);
+int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
+                   const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                   int act, int dtype, cudaStream_t st, float norm_eps, const void* wpk,
+                   const void* xpk, void* ypk);
 constexpr int64_t kDecodeMaxM = 64;
 }  // namespace tpp
 
@@ -55,4 +64,53 @@ extern "C" int tpp_rmsnorm_linear(const void* x, int64_t ldx, const void* w_fold
               "x and W rows must be 16-byte aligned (K and ldx multiples of 8)");
   return linear_decode(x, ldx, w_folded, bias, residual, y, ldy, M, N, K, act, dtype,
                        as_stream(stream), eps);
+}
+
+extern "C" int64_t tpp_packed_weight_bytes(int64_t N, int64_t K, int act) {
+  if (N <= 0 || K <= 0 || N > 0x3fffffff || K > 0x7fffffff) return 0;
+  return xs_packed_weight_bytes(N, K, act);
+}
+
+extern "C" int64_t tpp_packed_activation_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || M > 32 || K <= 0 || K > 0x7fffffff) return 0;
+  return xs_packed_activation_bytes(M, K);
+}
+
+extern "C" int tpp_pack_weight(const void* w, int64_t N, int64_t K, int act, int dtype,
+                               void* w_packed, void* stream) {
+  TPP_REQUIRE(w && w_packed, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(dtype == TPP_F16 || dtype == TPP_BF16, TPP_ERR_DTYPE, "dtype must be f16 or bf16");
+  TPP_REQUIRE(act >= TPP_ACT_NONE && act <= TPP_ACT_SWIGLU, TPP_ERR_UNSUPPORTED, "unknown activation");
+  TPP_REQUIRE(tpp_packed_weight_bytes(N, K, act) > 0, TPP_ERR_UNSUPPORTED,
+              "layer too wide for the packed form, or K not a multiple of 64");
+  TPP_REQUIRE(aligned16(w) && aligned16(w_packed), TPP_ERR_ALIGN, "16-byte alignment required");
+  return xs_pack_weight(w, N, K, act, w_packed, as_stream(stream));
+}
+
+extern "C" int tpp_pack_activation(const void* x, int64_t ldx, int64_t M, int64_t K, int dtype,
+                                   void* x_packed, void* stream) {
+  TPP_REQUIRE(x && x_packed, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(dtype == TPP_F16 || dtype == TPP_BF16, TPP_ERR_DTYPE, "dtype must be f16 or bf16");
+  TPP_REQUIRE(tpp_packed_activation_bytes(M, K) > 0 && ldx >= K, TPP_ERR_SHAPE,
+              "need 0 < M <= 32, K a multiple of 64, ldx >= K");
+  TPP_REQUIRE(ldx % 8 == 0 && aligned16(x) && aligned16(x_packed), TPP_ERR_ALIGN,
+              "16-byte alignment required");
+  return xs_pack_activation(x, ldx, M, K, x_packed, as_stream(stream));
+}
+
+extern "C" int tpp_linear_packed(const void* x_packed, const void* w_packed, const void* bias,
+                                 const void* residual, void* y, int64_t ldy, void* y_packed,
+                                 int64_t M, int64_t N, int64_t K, float eps, int act, int dtype,
+                                 void* stream) {
+  TPP_REQUIRE(x_packed && w_packed && y, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(M > 0 && M <= 32 && ldy >= N, TPP_ERR_SHAPE, "need 0 < M <= 32, ldy >= N");
+  TPP_REQUIRE(act >= TPP_ACT_NONE && act <= TPP_ACT_SWIGLU, TPP_ERR_UNSUPPORTED, "unknown activation");
+  TPP_REQUIRE(tpp_packed_weight_bytes(N, K, act) > 0, TPP_ERR_UNSUPPORTED,
+              "layer too wide for the packed form, or K not a multiple of 64");
+  TPP_REQUIRE(aligned16(x_packed) && aligned16(w_packed), TPP_ERR_ALIGN, "16-byte alignment required");
+  TPP_REQUIRE(!y_packed || (N % 64 == 0 && ldy % 8 == 0 && aligned16(y) && aligned16(y_packed) &&
+                            (!residual || aligned16(residual))),
+              TPP_ERR_ALIGN, "a packed output needs N % 64 == 0 and 16-byte aligned rows");
+  return linear_xs_impl(nullptr, K, nullptr, bias, residual, y, ldy, M, N, K, act, dtype,
+                        as_stream(stream), eps, w_packed, x_packed, y_packed);
 }

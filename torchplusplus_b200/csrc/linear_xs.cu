@@ -1,0 +1,674 @@
+// Decode-shaped linear layers, x-stationary form:
+//   y[M, N] = epilogue(x[M, K] . W[N, K]^T)      for M <= 32, N <= 64 x SMs.
+//
+// At decode the weights are read once per step and M is a handful of tokens.
+// Two measured B200 facts shape this kernel:
+//  * A tcgen05.mma costs ~180 SM clocks whatever its shape (M64 x N8 as much
+//    as M128 x N256), so with 32 tokens on one side the 5th-generation path
+//    runs at 1/8 of its rate and a CTA's chain of K/16 MMAs becomes the
+//    critical path.  Warp-level mma.sync m16n8k16 sustains ~1000 FMA/clock/SM
+//    from four warps with cost proportional to the work: ~3x faster for these
+//    tiles.  (Large GEMMs stay on tcgen05 in linear_tc.cu.)
+//  * A CTA's TMA throughput is set by its number of requests (~0.2 us each)
+//    more than by their size, so operands arrive in few large chunks.
+// Design:
+//  * Every CTA owns NR complete output rows (NR = N / SMs rounded up to 8,
+//    <= 64): no split-K, no cross-CTA reduction.  The tokens are the MMA's M
+//    side (16 or 32), the CTA's weight rows its N side.
+//  * One producer warp streams chunks of KC 64-wide k-blocks: the weight part
+//    as one 3-D TMA box {64, NR, KC} (or one bulk copy from a packed image),
+//    the x part as one box {64, T, KC} (or a bulk copy of packed x), into a
+//    ring of full/empty mbarriers.  The weight parts of the first `stages`
+//    chunks are requested before the programmatic-dependent-launch wait.
+//  * Four compute warps: warp w takes k16 step w of every k-block (ldmatrix
+//    from the 128-byte-swizzled tiles, conflict-free), accumulating all
+//    tokens x rows in registers; a shared-memory reduction over the warps
+//    precedes the epilogue.
+//  * SwiGLU: the weight part of each k-block holds G gate rows then the G
+//    matching up rows (a 4-D box over W viewed as [2][N][K]).
+//  * Fused RMSNorm (norm weight folded into W): each token's sum of squares
+//    comes from the A fragments the MMAs already load.
+//  * Epilogue: bias, activation / SwiGLU, residual (prefetched into shared
+//    memory while the weights stream), 16-byte stores, optionally a second
+//    packed copy of y for the next decode linear.
+// Reference: csrc/blas/hgemv/hgemv_kernels.cuh:19-85 (one warp per row, fp16
+// accumulation, never built) and the CUTLASS Sm80 fused linear of
+// csrc/activation/fused_gemm.cuh:143-170.  Accumulation here is fp32.
+#include "tc_common.cuh"
+#include "mma_common.cuh"
+
+namespace tpp {
+namespace {
+
+constexpr int kCompute = 8;                    // compute warps
+constexpr int kThreads = (kCompute + 1) * 32;  // + the producer warp
+constexpr int kMaxNT = 8;                      // 8-row n-tiles per CTA (NR <= 64)
+// Register tiles are sized for NTM n-tiles (2, 4 or 8).  Up to 4 the kernel
+// fits two CTAs per SM, so the next kernel's CTA can be resident (and
+// prefetch its weights) while this one finishes.
+constexpr int kMaxStages = 4;
+constexpr size_t kBudget = 110 * 1024;  // two CTAs (of two kernels) per SM
+
+struct XsArgs {
+  const void* bias;
+  const void* residual;
+  void* y;
+  int64_t ldy;
+  int M, N, K;
+  int act;
+  int nr;      // weight rows per CTA (SwiGLU: gate rows + up rows)
+  int kc;      // k-blocks per chunk
+  int nch;     // chunks
+  int stages;  // ring depth
+  int vec_ok;
+  float eps;   // fused RMSNorm (NORM variant)
+  int* err;
+  // Packed operands (optional): W as per-CTA images [cta][kb][NR][128 B] and
+  // x / y as [kb][T][128 B], both in the 128-byte-swizzled order the kernel
+  // stages, so every chunk is one contiguous bulk copy.
+  const uint8_t* wpk;
+  const uint8_t* xpk;
+  uint8_t* ypk;
+  int allow_wide;  // host-side choice only (see xs_dispatch)
+#ifdef TPP_DEBUG_STAMPS
+  unsigned dbg_id;
+#endif
+};
+
+#ifdef TPP_DEBUG_STAMPS
+// [launch % 64][cta < 256][16] globaltimer stamps
+__device__ unsigned long long g_xs_stamps[64 * 256 * 16];
+unsigned g_xs_launch = 0;
+#define XS_TS(i) do { if (blockIdx.x < 256) { unsigned long long _t; \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(_t)); \
+    g_xs_stamps[((p.dbg_id % 64) * 256 + blockIdx.x) * 16 + (i)] = _t; } } while (0)
+#else
+#define XS_TS(i) do {} while (0)
+#endif
+
+template <int BN>
+struct XsPlan {
+  __host__ __device__ static uint32_t stage(int nr, int kc) { return (uint32_t)(nr + BN) * kc * 128; }
+  __host__ __device__ static uint32_t red(int nr) { return (uint32_t)kCompute * BN * (nr + 4) * 4; }
+  static uint32_t rsd(int nro) { return ((uint32_t)BN * nro * 2 + 15) & ~15u; }
+  __host__ __device__ static size_t ring(int nr, int kc, int stages) {
+    const size_t r = (size_t)stages * stage(nr, kc);
+    return r > red(nr) ? r : red(nr);
+  }
+  static size_t smem(int nr, int nro, int kc, int stages) {
+    return 1024 + ring(nr, kc, stages) + 2048 + rsd(nro);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float sq2(uint32_t v) {
+  float2 f;
+  if constexpr (IsBf16<T>::value) f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+  else f = __half22float2(*reinterpret_cast<__half2*>(&v));
+  return f.x * f.x + f.y * f.y;
+}
+
+template <typename T, int BN, int NTM, bool SWIGLU, bool NORM>
+__global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
+    linear_xs_kernel(const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_x, XsArgs p) {
+  constexpr int MT = BN / 16;  // m-tiles (16 tokens)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  const int NR = p.nr, KC = p.kc, S = p.stages, NCH = p.nch;
+  const int NRO = SWIGLU ? NR / 2 : NR;  // outputs per CTA
+  const int NT = NR / 8;                 // n-tiles
+  const int RST = NR + 4;                // row stride of the reduction buffer
+  const uint32_t wbytes = (uint32_t)NR * KC * 128;
+  const uint32_t xbytes = (uint32_t)BN * KC * 128;
+  const uint32_t sbytes = wbytes + xbytes;
+  uint8_t* misc = smem + XsPlan<BN>::ring(NR, KC, S);
+  uint64_t* full = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* empty = full + kMaxStages;
+  float* ssw = reinterpret_cast<float*>(misc + 128);  // [kCompute][BN] sums of squares (1 KB)
+  T* rsd = reinterpret_cast<T*>(misc + 2048);         // [BN][NRO] residual slice
+  float* red = reinterpret_cast<float*>(smem);        // [kCompute][BN][RST], after the ring
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * NRO;  // first output (and weight row) of this CTA
+  const int nkb = (p.K + 63) / 64;
+  const int mt = p.M < BN ? p.M : BN;
+
+#ifdef TPP_DEBUG_STAMPS
+  const unsigned long long clk0 = clock64();
+#endif
+  if (threadIdx.x == 0) {
+    XS_TS(0);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCompute);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kCompute) {
+    // ---------------- TMA / bulk producer ----------------
+    if (lane != 0) return;
+    bool ok = true;
+    auto kbc = [&](int c) { return nkb - c * KC < KC ? nkb - c * KC : KC; };
+    auto tx_bytes = [&](int c) {
+      return (p.wpk ? (uint32_t)kbc(c) * NR * 128 : wbytes) +
+             (p.xpk ? (uint32_t)kbc(c) * BN * 128 : xbytes);
+    };
+    auto load_w = [&](int c) {
+      uint8_t* dst = smem + (c % S) * sbytes;
+      if (p.wpk)
+        bulk_load(dst, p.wpk + ((size_t)blockIdx.x * nkb + (size_t)c * KC) * NR * 128,
+                  (uint32_t)kbc(c) * NR * 128, &full[c % S]);
+      else if (SWIGLU)
+        tma_load_4d(dst, &tm_w, &full[c % S], 0, row0, 0, c * KC);
+      else
+        tma_load_3d(dst, &tm_w, &full[c % S], 0, row0, c * KC);
+    };
+    auto load_x = [&](int c) {
+      uint8_t* dst = smem + (c % S) * sbytes + wbytes;
+      if (p.xpk)
+        bulk_load(dst, p.xpk + (size_t)c * KC * BN * 128, (uint32_t)kbc(c) * BN * 128,
+                  &full[c % S]);
+      else
+        tma_load_3d(dst, &tm_x, &full[c % S], 0, 0, c * KC);
+    };
+    XS_TS(4);
+    if (!p.wpk) prefetch_tmap(&tm_w);
+    if (!p.xpk) prefetch_tmap(&tm_x);
+    XS_TS(5);
+    const int pre = NCH < S ? NCH : S;
+    for (int c = 0; c < pre; ++c) {
+      mbar_arrive_expect_tx(&full[c], tx_bytes(c));
+      load_w(c);  // weights: independent of the previous kernel
+    }
+    XS_TS(12);
+    pdl_wait();
+    XS_TS(13);
+    pdl_trigger();
+    for (int c = 0; c < pre; ++c) load_x(c);
+    for (int c = pre; c < NCH && ok; ++c) {
+      const int s = c % S;
+      ok = mbar_wait(&empty[s], ((c / S) & 1) ^ 1, p.err, 21);
+      if (!ok) break;
+      mbar_arrive_expect_tx(&full[s], tx_bytes(c));
+      load_w(c);
+      load_x(c);
+    }
+    return;
+  }
+
+  // ---------------- compute warps ----------------
+  pdl_wait();
+  if (threadIdx.x == 0) XS_TS(1);
+  const int tid = threadIdx.x;  // 0 .. 127
+  if (p.residual && p.vec_ok) {
+    const T* res = static_cast<const T*>(p.residual);
+    const int chunks = NRO / 8;
+    for (int e = tid; e < mt * chunks; e += kCompute * 32) {
+      const int t = e / chunks, ch = e % chunks;
+      const int n0 = row0 + ch * 8;
+      if (n0 + 8 <= p.N)
+        *reinterpret_cast<uint4*>(rsd + t * NRO + ch * 8) =
+            *reinterpret_cast<const uint4*>(res + (int64_t)t * p.ldy + n0);
+    }
+  }
+  float acc[MT][NTM][4];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < NTM; ++ni)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[mi][ni][q] = 0.f;
+  float ssl[MT][2] = {};
+  bool ok = true;
+  // Warp w takes k16 step (w % 4) of every (kCompute / 4)-th k-block of each
+  // chunk; the fragments of its next k-block load while the current MMAs run.
+  constexpr int kJStep = kCompute / 4;  // k-block stride of one warp
+  const int kk = warp & 3, jpar = warp >> 2;
+  // Per-thread ldmatrix offsets inside a k-block tile (constant: this warp
+  // always reads the same k16 step); 128-byte swizzle: 16-byte chunk q of
+  // row r sits at position q ^ (r % 8).
+  uint32_t offa[MT], offb[NTM / 2];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi) {
+    const int row = mi * 16 + (lane & 15);
+    const int ch = kk * 2 + (lane >> 4);
+    offa[mi] = (uint32_t)(row * 128 + ((ch ^ (row & 7)) << 4));
+  }
+#pragma unroll
+  for (int np = 0; np < NTM / 2; ++np) {
+    // n-tiles 2np and 2np+1 (the second clamped to the first when NT is odd)
+    const int nt = (2 * np + 1 < NT) ? 2 * np + ((lane >> 4) & 1) : 2 * np;
+    const int n = nt * 8 + (lane & 7);
+    const int ch = kk * 2 + ((lane >> 3) & 1);
+    offb[np] = (uint32_t)(n * 128 + ((ch ^ (n & 7)) << 4));
+  }
+  const uint32_t xstride = BN * 128, wstride = (uint32_t)NR * 128;  // bytes per k-block tile
+  auto load_frags = [&](uint32_t ws, uint32_t xs, int j, uint32_t (&a)[MT][4],
+                        uint32_t (&b)[NTM / 2][4]) {
+    const uint32_t xj = xs + j * xstride, wj = ws + j * wstride;
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xj + offa[mi], a[mi]);
+#pragma unroll
+    for (int np = 0; np < NTM / 2; ++np) {
+      if (2 * np >= NT) break;
+      ldsm_x4(wj + offb[np], b[np]);
+    }
+  };
+  for (int c = 0; c < NCH && ok; ++c) {
+    const int s = c % S;
+    ok = mbar_wait(&full[s], (c / S) & 1, p.err, 22);
+    if (!ok) break;
+    if (threadIdx.x == 0 && c < 2) XS_TS(2 + c);
+    const uint32_t ws = smem_u32(smem + s * sbytes);
+    const uint32_t xs = ws + wbytes;
+    const int nj = nkb - c * KC < KC ? nkb - c * KC : KC;
+    uint32_t a0[MT][4], b0[NTM / 2][4], a1[MT][4], b1[NTM / 2][4];
+    auto mmas = [&](const uint32_t (&a)[MT][4], const uint32_t (&b)[NTM / 2][4]) {
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) {
+        if (NORM) {
+          ssl[mi][0] += sq2<T>(a[mi][0]) + sq2<T>(a[mi][2]);
+          ssl[mi][1] += sq2<T>(a[mi][1]) + sq2<T>(a[mi][3]);
+        }
+#pragma unroll
+        for (int np = 0; np < NTM / 2; ++np) {
+          if (2 * np >= NT) break;
+          mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+          if (2 * np + 1 < NT) mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+        }
+      }
+    };
+    int j = jpar;
+    if (j < nj) load_frags(ws, xs, j, a0, b0);
+    while (j < nj) {
+      if (j + kJStep < nj) load_frags(ws, xs, j + kJStep, a1, b1);
+      mmas(a0, b0);
+      j += kJStep;
+      if (j >= nj) break;
+      if (j + kJStep < nj) load_frags(ws, xs, j + kJStep, a0, b0);
+      mmas(a1, b1);
+      j += kJStep;
+    }
+    __syncwarp();
+    if (threadIdx.x == 0 && c == 0) XS_TS(14);
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---------------- cross-warp reduction ----------------
+  if (threadIdx.x == 0) XS_TS(8);
+  asm volatile("bar.sync 1, %0;" ::"n"(kCompute * 32) : "memory");  // ring no longer read
+  if (threadIdx.x == 0) XS_TS(9);
+  {
+    const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+#pragma unroll
+      for (int ni = 0; ni < NTM; ++ni) {
+        if (ni >= NT) break;
+        const int n = ni * 8 + cq * 2;
+        float* r0 = red + (warp * BN + mi * 16 + g) * RST + n;
+        float* r1 = r0 + 8 * RST;
+        r0[0] = acc[mi][ni][0]; r0[1] = acc[mi][ni][1];
+        r1[0] = acc[mi][ni][2]; r1[1] = acc[mi][ni][3];
+      }
+      if (NORM) {
+        float lo = ssl[mi][0], hi = ssl[mi][1];
+        lo += __shfl_xor_sync(0xffffffffu, lo, 1);
+        lo += __shfl_xor_sync(0xffffffffu, lo, 2);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 1);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 2);
+        if (cq == 0) {
+          ssw[warp * BN + mi * 16 + g] = lo;
+          ssw[warp * BN + mi * 16 + g + 8] = hi;
+        }
+      }
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kCompute * 32) : "memory");
+  if (threadIdx.x == 0) XS_TS(10);
+
+  // ---------------- epilogue ----------------
+  const T* bias = static_cast<const T*>(p.bias);
+  const T* res = static_cast<const T*>(p.residual);
+  T* Y = static_cast<T*>(p.y);
+  const int groups = NRO / 8;
+  const float inv_k = 1.0f / (float)p.K;
+  for (int e = tid; e < mt * groups; e += kCompute * 32) {
+    const int t = e / groups, c0 = (e % groups) * 8;
+    const int n0 = row0 + c0;
+    if (n0 >= p.N) continue;
+    float rs = 1.f;
+    if (NORM) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCompute; ++w) ss += ssw[w * BN + t];
+      rs = rsqrtf(ss * inv_k + p.eps);
+    }
+    if (threadIdx.x == 0) XS_TS(6);
+    float g8[8], u8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { g8[i] = 0.f; u8[i] = 0.f; }
+#pragma unroll
+    for (int w = 0; w < kCompute; ++w) {
+      const float* rr = red + (w * BN + t) * RST + c0;
+      const float4 p0 = *reinterpret_cast<const float4*>(rr);
+      const float4 p1 = *reinterpret_cast<const float4*>(rr + 4);
+      g8[0] += p0.x; g8[1] += p0.y; g8[2] += p0.z; g8[3] += p0.w;
+      g8[4] += p1.x; g8[5] += p1.y; g8[6] += p1.z; g8[7] += p1.w;
+      if (SWIGLU) {
+        const float4 q0 = *reinterpret_cast<const float4*>(rr + NRO);
+        const float4 q1 = *reinterpret_cast<const float4*>(rr + NRO + 4);
+        u8[0] += q0.x; u8[1] += q0.y; u8[2] += q0.z; u8[3] += q0.w;
+        u8[4] += q1.x; u8[5] += q1.y; u8[6] += q1.z; u8[7] += q1.w;
+      }
+    }
+    if (threadIdx.x == 0) XS_TS(7);
+    float o[8];
+    const bool vec = p.vec_ok && n0 + 8 <= p.N;
+    if (bias && vec) {
+      float bg[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(bias + n0), bg);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) g8[i] = g8[i] * rs + bg[i];
+      if (SWIGLU) {
+        unpack8<T>(*reinterpret_cast<const uint4*>(bias + p.N + n0), bg);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u8[i] = u8[i] * rs + bg[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const bool in = bias && n0 + i < p.N;
+        g8[i] = g8[i] * rs + (in ? to_f32(bias[n0 + i]) : 0.f);
+        if (SWIGLU) u8[i] = u8[i] * rs + (in ? to_f32(bias[p.N + n0 + i]) : 0.f);
+      }
+    }
+    if (SWIGLU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = act_silu(g8[i]) * u8[i];
+    } else if (p.act == TPP_ACT_SILU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = act_silu(g8[i]);
+    } else if (p.act == TPP_ACT_GELU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = act_gelu_tanh(g8[i]);
+    } else if (p.act == TPP_ACT_RELU) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = act_relu(g8[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = g8[i];
+    }
+    T* yr = Y + (int64_t)t * p.ldy;
+    if (vec) {
+      if (res) {
+        float rf[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(rsd + t * NRO + c0), rf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] += rf[i];
+      }
+      const uint4 pk = pack8<T>(o);
+      *reinterpret_cast<uint4*>(yr + n0) = pk;
+      if (p.ypk)  // packed copy for the next decode linear: [kb][T][128 B], swizzled
+        *reinterpret_cast<uint4*>(p.ypk + ((size_t)(n0 >> 6) * BN + t) * 128 +
+                                  ((((n0 >> 3) & 7) ^ (t & 7)) << 4)) = pk;
+    } else {
+      const T* rr = res ? res + (int64_t)t * p.ldy : nullptr;
+      for (int i = 0; i < 8 && n0 + i < p.N; ++i) {
+        float v = o[i];
+        if (rr) v += to_f32(rr[n0 + i]);
+        yr[n0 + i] = from_f32<T>(v);
+      }
+    }
+  }
+  if (threadIdx.x == 0) XS_TS(11);
+#ifdef TPP_DEBUG_STAMPS
+  if (threadIdx.x == 0 && blockIdx.x < 256)
+    g_xs_stamps[((p.dbg_id % 64) * 256 + blockIdx.x) * 16 + 15] = clock64() - clk0;
+#endif
+}
+
+template <typename T, int BN, int NTM, bool SW, bool NORM>
+int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
+              int nro) {
+  using Plan = XsPlan<BN>;
+  const int nr = SW ? 2 * nro : nro;
+  const int nkb = (a.K + 63) / 64;
+  // chunk: as many k-blocks as keep two stages within the budget, x part <= 32 KB
+  int kc = 8;
+  if (kc > nkb) kc = nkb;
+  while (kc > 1 && (BN * kc * 128 > 32768 || Plan::smem(nr, nro, kc, 2) > kBudget)) --kc;
+  if (Plan::smem(nr, nro, kc, nkb > kc ? 2 : 1) > kBudget) return -1;  // not applicable
+  const int nch = (nkb + kc - 1) / kc;
+  int stages = nch < kMaxStages ? nch : kMaxStages;
+  while (stages > 1 && Plan::smem(nr, nro, kc, stages) > kBudget) --stages;
+  a.nr = nr; a.kc = kc; a.nch = nch; a.stages = stages;
+#ifdef TPP_DEBUG_STAMPS
+  a.dbg_id = g_xs_launch++;
+#endif
+
+  CUtensorMap tw, tx;
+  if (a.wpk) {
+    // unused by the kernel (bulk copies), but a valid map keeps the launch uniform
+    const uint64_t dims[2] = {64, 8};
+    const uint64_t strides[1] = {128};
+    const uint32_t box[2] = {64, 8};
+    const int rc = make_tmap(&tw, a.wpk, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  } else if (SW) {
+    // W [2N][K] as {k in block, row, half, k-block}
+    const uint64_t dims[4] = {64, (uint64_t)a.N, 2, (uint64_t)nkb};
+    const uint64_t strides[3] = {(uint64_t)a.K * 2, (uint64_t)a.N * a.K * 2, 128};
+    const uint32_t box[4] = {64, (uint32_t)nro, 2, (uint32_t)kc};
+    const int rc = make_tmap(&tw, w, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  } else {
+    const uint64_t dims[3] = {64, (uint64_t)a.N, (uint64_t)nkb};
+    const uint64_t strides[2] = {(uint64_t)a.K * 2, 128};
+    const uint32_t box[3] = {64, (uint32_t)nr, (uint32_t)kc};
+    const int rc = make_tmap(&tw, w, dtype, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  }
+  if (a.xpk) {
+    const uint64_t dims[2] = {64, 8};
+    const uint64_t strides[1] = {128};
+    const uint32_t box[2] = {64, 8};
+    const int rc = make_tmap(&tx, a.xpk, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  } else {
+    const uint64_t dims[3] = {64, (uint64_t)a.M, (uint64_t)nkb};
+    const uint64_t strides[2] = {(uint64_t)ldx * 2, 128};
+    const uint32_t box[3] = {64, (uint32_t)BN, (uint32_t)kc};
+    const int rc = make_tmap(&tx, x, dtype, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  }
+  const int ctas = (a.N + nro - 1) / nro;
+  auto kern = linear_xs_kernel<T, BN, NTM, SW, NORM>;
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBudget) != cudaSuccess) {
+      set_error("linear_xs_kernel: cannot reserve shared memory");
+      return TPP_ERR_LAUNCH;
+    }
+    configured |= bit;
+  }
+  return launch("linear_xs_kernel", kern, dim3((unsigned)ctas), dim3(kThreads),
+                Plan::smem(nr, nro, kc, stages), st, 1u, tw, tx, a);
+}
+
+template <typename T, int NTM, bool NORM>
+int xs_dispatch_nt(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype,
+                   cudaStream_t st, int nro) {
+  const bool sw = a.act == TPP_ACT_SWIGLU;
+  if (a.M <= 16)
+    return sw ? launch_xs<T, 16, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro)
+              : launch_xs<T, 16, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro);
+  if (a.M <= 32)
+    return sw ? launch_xs<T, 32, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro)
+              : launch_xs<T, 32, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro);
+  return -1;
+}
+
+template <typename T, bool NORM>
+int xs_dispatch(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
+                int nro) {
+  const int nt = (a.act == TPP_ACT_SWIGLU ? 2 * nro : nro) / 8;
+  if (nt <= 2) return xs_dispatch_nt<T, 2, NORM>(x, ldx, w, a, dtype, st, nro);
+  if (nt <= 4) return xs_dispatch_nt<T, 4, NORM>(x, ldx, w, a, dtype, st, nro);
+  // Wider slices only fit one CTA per SM, which also keeps the next kernel's
+  // CTAs from starting early; the packed entry point still takes them, the
+  // plain decode dispatch prefers the weight-streaming kernel (a.allow_wide).
+  if (!a.allow_wide) return -1;
+  return xs_dispatch_nt<T, 8, NORM>(x, ldx, w, a, dtype, st, nro);
+}
+
+}  // namespace
+
+
+// Decode linear in x-stationary form.  Returns -1 (nothing launched) when the
+// shape is better served by the weight-streaming kernel (very wide N, or a
+// slice that does not fit the shared-memory budget); otherwise a TPP status.
+#ifdef TPP_DEBUG_STAMPS
+extern "C" void tpp_debug_xs_stamps(unsigned long long* host) {
+  cudaMemcpyFromSymbol(host, g_xs_stamps, sizeof(unsigned long long) * 64 * 256 * 16);
+}
+extern "C" unsigned tpp_debug_xs_launches() { return g_xs_launch; }
+#endif
+
+// Outputs per CTA (SwiGLU CTAs hold that many gate rows plus as many up
+// rows) for an N-wide layer on this device, or 0 when N is too wide.
+int xs_outputs_per_cta(int64_t N, int act) {
+  const int sms = num_sms();
+  int64_t nro = (N + sms - 1) / sms;
+  nro = (nro + 7) / 8 * 8;
+  const int64_t nr = act == TPP_ACT_SWIGLU ? 2 * nro : nro;
+  return nr > 8 * kMaxNT ? 0 : (int)nro;
+}
+int xs_token_tile(int64_t M) { return M <= 16 ? 16 : 32; }
+
+int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
+                   const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                   int act, int dtype, cudaStream_t st, float norm_eps, const void* wpk,
+                   const void* xpk, void* ypk) {
+  // The 3-D views address k-block kb of a row at +128 * kb bytes: rows must
+  // be whole k-blocks, or the last one would run into the next row.
+  if (K % 64 != 0 || M > 32) return -1;
+  const int nro = xs_outputs_per_cta(N, act);
+  if (nro == 0) return -1;
+  XsArgs a;
+  a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
+  a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act;
+  a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned16(y) &&
+             (!residual || aligned16(residual)) && (!bias || aligned16(bias));
+  a.eps = norm_eps;
+  a.err = device_error_flag();
+  a.wpk = static_cast<const uint8_t*>(wpk);
+  a.xpk = static_cast<const uint8_t*>(xpk);
+  a.ypk = static_cast<uint8_t*>(ypk);
+  a.allow_wide = wpk != nullptr;
+  return TPP_DISPATCH_HALF(dtype, T, [&] {
+    return norm_eps >= 0.f ? xs_dispatch<T, true>(x, ldx, w, a, dtype, st, nro)
+                           : xs_dispatch<T, false>(x, ldx, w, a, dtype, st, nro);
+  });
+}
+
+}  // namespace tpp
+
+namespace tpp {
+
+int linear_xs(const void* x, int64_t ldx, const void* w, const void* bias, const void* residual,
+              void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int act, int dtype,
+              cudaStream_t st, float norm_eps) {
+  return linear_xs_impl(x, ldx, w, bias, residual, y, ldy, M, N, K, act, dtype, st, norm_eps,
+                        nullptr, nullptr, nullptr);
+}
+
+namespace {
+// W [N or 2N][K] -> per-CTA images [cta][kb][NR][128 B]; 16-byte chunk j of
+// image row rr is stored at position j ^ (rr % 8) (128-byte swizzle).  Rows
+// past N are zero.
+__global__ void pack_weight_kernel(const uint8_t* __restrict__ w, int N, int K, int nro, int nr,
+                                   int swiglu, int64_t total, uint8_t* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
+  const int nkb = K / 64;
+  for (int64_t id = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; id < total;
+       id += (int64_t)gridDim.x * blockDim.x) {
+    const int pos = (int)(id & 7);
+    const int64_t q = id >> 3;
+    const int rr = (int)(q % nr);
+    const int64_t q2 = q / nr;
+    const int kb = (int)(q2 % nkb);
+    const int64_t cta = q2 / nkb;
+    const int j = pos ^ (rr & 7);
+    int64_t grow;
+    bool valid;
+    if (swiglu) {
+      const int g = nr / 2;
+      const int64_t r = cta * g + rr % g;
+      valid = r < N;
+      grow = (rr / g) * (int64_t)N + r;
+    } else {
+      grow = cta * nro + rr;
+      valid = grow < N;
+    }
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (valid) v = *reinterpret_cast<const uint4*>(w + (grow * K + kb * 64 + j * 8) * 2);
+    *reinterpret_cast<uint4*>(dst + id * 16) = v;
+  }
+}
+// x [M][K] -> [kb][BN][128 B], swizzled like the weights; rows >= M are zero.
+__global__ void pack_activation_kernel(const uint8_t* __restrict__ x, int64_t ldx, int M, int K,
+                                       int bn, int64_t total, uint8_t* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t id = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; id < total;
+       id += (int64_t)gridDim.x * blockDim.x) {
+    const int pos = (int)(id & 7);
+    const int t = (int)((id >> 3) % bn);
+    const int kb = (int)((id >> 3) / bn);
+    const int j = pos ^ (t & 7);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < M) v = *reinterpret_cast<const uint4*>(x + (t * ldx + kb * 64 + j * 8) * 2);
+    *reinterpret_cast<uint4*>(dst + id * 16) = v;
+  }
+}
+}  // namespace
+
+int64_t xs_packed_weight_bytes(int64_t N, int64_t K, int act) {
+  if (K % 64 != 0) return 0;
+  const int nro = xs_outputs_per_cta(N, act);
+  if (nro == 0) return 0;
+  const int64_t nr = act == TPP_ACT_SWIGLU ? 2 * nro : nro;
+  return (N + nro - 1) / nro * (K / 64) * nr * 128;
+}
+int64_t xs_packed_activation_bytes(int64_t M, int64_t K) {
+  return K % 64 != 0 ? 0 : (K / 64) * xs_token_tile(M) * 128;
+}
+int xs_pack_weight(const void* w, int64_t N, int64_t K, int act, void* dst, cudaStream_t st) {
+  const int nro = xs_outputs_per_cta(N, act);
+  const int nr = act == TPP_ACT_SWIGLU ? 2 * nro : nro;
+  const int64_t total = xs_packed_weight_bytes(N, K, act) / 16;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  return launch("pack_weight_kernel", pack_weight_kernel, dim3(blocks), dim3(256), 0, st, 1u,
+                static_cast<const uint8_t*>(w), (int)N, (int)K, nro, nr,
+                act == TPP_ACT_SWIGLU ? 1 : 0, total, static_cast<uint8_t*>(dst));
+}
+int xs_pack_activation(const void* x, int64_t ldx, int64_t M, int64_t K, void* dst,
+                       cudaStream_t st) {
+  const int64_t total = xs_packed_activation_bytes(M, K) / 16;
+  const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
+  return launch("pack_activation_kernel", pack_activation_kernel, dim3(blocks), dim3(256), 0,
+                st, 1u, static_cast<const uint8_t*>(x), ldx, (int)M, (int)K, xs_token_tile(M),
+                total, static_cast<uint8_t*>(dst));
+}
+
+}  // namespace tpp

@@ -217,6 +217,69 @@ def rmsnorm_linear(x: torch.Tensor, w_folded: torch.Tensor, eps: float = 1e-6,
     return out
 
 
+class PackedWeight:
+    """A decode-linear weight re-laid out once (tpp_pack_weight) into the
+    per-CTA, swizzled tiles the packed kernel copies with contiguous bulk
+    loads.  `n` = outputs, `k` = inputs, `act` as for linear()."""
+
+    def __init__(self, weight: torch.Tensor, act: str = "none"):
+        _cuda(weight)
+        dt = _half(weight, "weight")
+        rows, K = weight.shape
+        Nout = rows // 2 if act == "swiglu" else rows
+        code = N.ACT_CODE[act]
+        nbytes = N.lib().tpp_packed_weight_bytes(Nout, K, code)
+        if nbytes <= 0:
+            raise ValueError("layer does not fit the packed decode form "
+                             "(K must be a multiple of 64, N at most 256 per SM)")
+        w = weight.contiguous()
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=weight.device)
+        N.call("tpp_pack_weight", w.data_ptr(), Nout, K, code, dt, self.data.data_ptr(),
+               N.stream_of(weight))
+        self.n, self.k, self.act, self.dtype = Nout, K, act, weight.dtype
+
+    @staticmethod
+    def supported(n: int, k: int, act: str = "none") -> bool:
+        return N.lib().tpp_packed_weight_bytes(n, k, N.ACT_CODE[act]) > 0
+
+
+def packed_activation_bytes(M: int, K: int) -> int:
+    return int(N.lib().tpp_packed_activation_bytes(M, K))
+
+
+def pack_activation(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [M, K] (M <= 64) -> packed activation bytes for linear_packed."""
+    _cuda(x, out)
+    dt = _half(x, "x")
+    M, K = x.shape
+    nbytes = packed_activation_bytes(M, K)
+    if nbytes <= 0:
+        raise ValueError("need 0 < M <= 64 and K a multiple of 64")
+    if out is None:
+        out = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    x2 = x if x.stride(-1) == 1 and x.stride(0) % 8 == 0 else x.contiguous()
+    N.call("tpp_pack_activation", x2.data_ptr(), x2.stride(0), M, K, dt, out.data_ptr(),
+           N.stream_of(x))
+    return out
+
+
+def linear_packed(x_packed: torch.Tensor, M: int, w: PackedWeight,
+                  bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                  eps: float | None = None, out: torch.Tensor | None = None,
+                  out_packed: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode linear on packed operands: y[M, n] = act(scale * x.W^T + bias)
+    + residual, scale = rsqrt(mean(x^2) + eps) when eps is given (w packed from
+    the norm-folded matrix).  out_packed receives y packed for the next layer."""
+    _cuda(x_packed, bias, residual, out, out_packed)
+    dt = 1 if w.dtype == torch.bfloat16 else 0
+    if out is None:
+        out = torch.empty((M, w.n), dtype=w.dtype, device=x_packed.device)
+    N.call("tpp_linear_packed", x_packed.data_ptr(), w.data.data_ptr(), N.ptr(bias),
+           N.ptr(residual), out.data_ptr(), out.stride(0), N.ptr(out_packed), M, w.n, w.k,
+           -1.0 if eps is None else float(eps), N.ACT_CODE[w.act], dt, N.stream_of(x_packed))
+    return out
+
+
 def hgemv(weight: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """y[N] = weight[N,K] @ x[K] with fp32 accumulation."""
     _cuda(weight, x)
