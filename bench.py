@@ -11,7 +11,7 @@ larger than L2, so no L2 flush is needed between steps.
            of the summed decode time (CUDA events on the launch stream).
   e2e    = tokens/s through the public API Qwen3.generate(host ids) -- prompt
            H2D copy, prefill, 256 decode steps, result D2H copy all timed.
-  roofline = the decode linear kernel (dominant: streams every weight once per
+  roofline = the decode linear kernels (dominant: stream every weight once per
            step), timed alone as a CUDA-graph replay of all 113 linear
            launches of one step; bytes = weights + activations.
   cpu_baseline = the fp32 PyTorch-eager oracle (the reference's eager
@@ -40,6 +40,12 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tokens/sec (Qwen3-0.6B shape) at 1/2/4/8 B200; per-op % of HBM/TC roofline"
 PROMPT, GEN = 512, 256
+
+
+# DRAM bytes (read + write) per decode-linear launch, measured by ncu on this
+# bench's own command (profiles/decode_linears_dram_qwen3_b32.md): 10.797 MB
+# against 10.93 MB algorithmic -- the weights are read once.
+LINEAR_DRAM_BYTES_PER_LAUNCH = 10.797e6
 
 
 def peaks():
@@ -382,10 +388,15 @@ def run_ours(args, rank, world, local):
     rl = linear_roofline(eng)
     peak, peak_kind = peaks()
     achieved = rl["bytes_per_launch"] / rl["avg_launch_s"] / 1e9
-    roofline = {"kernel": "linear_skinny_kernel (all decode-step linears incl. LM head)",
+    roofline = {"kernel": "decode linears: linear_xs_kernel (qkv, o, down) and "
+                          "linear_skinny_kernel (gate/up, LM head), 113 launches per step",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind}",
-                "traffic": None, "bytes_per_launch": rl["bytes_per_launch"],
+                "traffic": LINEAR_DRAM_BYTES_PER_LAUNCH,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one "
+                                  "decode step's 113 linear launches "
+                                  "(profiles/decode_linears_dram_qwen3_b32.md)",
+                "bytes_per_launch": rl["bytes_per_launch"],
                 "avg_launch_us": rl["avg_launch_s"] * 1e6,
                 "step_linear_time_us": rl["seconds"] * 1e6}
     extra = {}
