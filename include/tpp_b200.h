@@ -208,6 +208,25 @@ int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
                          int64_t window_left, float scale, void* workspace,
                          int64_t workspace_bytes, int dtype, void* stream);
 
+/* Decode attention with the step's q/k RMSNorm + RoPE + KV append fused in:
+ * one launch replaces tpp_qk_norm_rope_cache (S = 1) + tpp_attention_decode.
+ * qkv[b] is the raw QKV projection row [q (Hq*D) | k (Hkv*D) | v (Hkv*D)]
+ * (row stride ld_qkv); q/k are normalised with qn_w / kn_w (either may be
+ * NULL = no norm) and rotated at positions[b] (fp16 tables [ctx, D], row
+ * stride cs_stride, NeoX rotate-half), the new k/v are written to the cache
+ * row positions[b], and attention covers keys [.., positions[b]].  Requires
+ * positions[b] == seqlens[b] - 1 and D = 64 or 128.  Other arguments as
+ * tpp_attention_decode.  Replaces the q_norm/k_norm + qkrope + KVCache.update
+ * + flash_attn_func sequence of torchpp/attention/gqa.py:96-128. */
+int tpp_attention_decode_qkv(const void* qkv, int64_t ld_qkv, const void* qn_w,
+                             const void* kn_w, float eps, const void* cos, const void* sin,
+                             int64_t cs_stride, int cs_dtype, const int32_t* positions,
+                             void* k_cache, void* v_cache, int64_t c_sb, int64_t c_sh,
+                             int64_t c_ss, const int32_t* seqlens, int64_t max_seqlen, void* o,
+                             int64_t o_sb, int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv,
+                             int64_t D, int64_t window_left, float scale, void* workspace,
+                             int64_t workspace_bytes, int dtype, void* stream);
+
 /* Allocation-free decode attention: the same computation and arguments as
  * tpp_attention_decode, minus the workspace.  For callers that cannot
  * allocate device memory when they decode (allocator / memory-pool

@@ -342,6 +342,60 @@ def test_qk_norm_rope_cache(dtype, S):
     assert kc[0, :, S:].abs().sum().item() == 0
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", [
+    # B, Hq, Hkv, D, lens (new token at lens-1), window, norms
+    (4, 16, 8, 128, [1, 64, 65, 700], -1, True),       # Qwen3-0.6B heads; first token
+    (3, 16, 8, 128, [513, 2000, 40], 255, True),       # sliding window
+    (2, 8, 1, 64, [129, 5], -1, False),                # MQA, D 64, no q/k norm
+    (8, 32, 4, 128, [300] * 8, -1, True),              # 8 query heads per kv head
+    (1, 64, 2, 128, [9000], -1, True),                 # G = 32: two head passes, many splits
+])
+def test_attention_decode_qkv_fused(dtype, case):
+    """One launch = q/k norm + RoPE + KV append + attention; checked against
+    the fp32 oracle and against the unfused two-kernel path."""
+    B, Hq, Hkv, D, lens, window, norms = case
+    g = gen(41)
+    Smax = max(lens) + 5
+    qkv = rnd(B, 1, (Hq + 2 * Hkv) * D, g=g, dtype=dtype)
+    qn = rnd(D, g=g, mean=1.0, std=0.1, dtype=dtype) if norms else None
+    kn = rnd(D, g=g, mean=1.0, std=0.1, dtype=dtype) if norms else None
+    cos, sin = O.compute_rope_params(D, 1e6, Smax)
+    kc0 = rnd(B, Hkv, Smax, D, g=g, dtype=dtype)
+    vc0 = rnd(B, Hkv, Smax, D, g=g, dtype=dtype)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    pos = sl - 1
+    d = lambda t: None if t is None else t.to(DEV)
+    kc, vc = kc0.to(DEV), vc0.to(DEV)
+    y = ops.attention_decode_qkv(qkv.to(DEV), d(qn), d(kn), 1e-6, cos.to(DEV), sin.to(DEV),
+                                 pos.to(DEV), kc, vc, sl.to(DEV), Smax, Hq, Hkv,
+                                 window_left=window)
+    # oracle: q/k normed + rotated, caches with the new row, decode attention
+    x = qkv.view(B, 1, Hq + 2 * Hkv, D)
+    p = pos[:, None, None]
+    qref = O.qk_norm_rope(x[:, :, :Hq], qn, 1e-6, cos, sin, p)
+    kref = O.qk_norm_rope(x[:, :, Hq:Hq + Hkv], kn, 1e-6, cos, sin, p)
+    kref_c, vref_c = kc0.float().clone(), vc0.float().clone()
+    for b in range(B):
+        kref_c[b, :, int(pos[b])] = kref[b, 0].to(dtype).float()
+        vref_c[b, :, int(pos[b])] = x[b, 0, Hq + Hkv:].float()
+    check(y, O.attention_decode(qref[:, 0].to(dtype), kref_c.to(dtype), vref_c.to(dtype), sl,
+                                window_left=window))
+    # the cache rows written by the fused launch match the oracle; others untouched
+    for b in range(B):
+        check(kc[b, :, int(pos[b])], kref[b, 0])
+        assert torch.equal(vc[b, :, int(pos[b])].cpu(), x[b, 0, Hq + Hkv:])
+        keep = torch.ones(Smax, dtype=torch.bool)
+        keep[int(pos[b])] = False
+        assert torch.equal(kc[b][:, keep].cpu(), kc0[b][:, keep])
+    # and the unfused path agrees
+    kc2, vc2 = kc0.to(DEV), vc0.to(DEV)
+    q2 = ops.qk_norm_rope_cache(qkv.to(DEV), d(qn), d(kn), 1e-6, cos.to(DEV), sin.to(DEV),
+                                pos.to(DEV), kc2, vc2, Hq, Hkv)
+    y2 = ops.attention_decode(q2.view(B, Hq, D), kc2, vc2, sl.to(DEV), Smax, window_left=window)
+    check(y, y2.float().cpu())
+
+
 def test_kv_append_and_kvcache():
     from torchplusplus_b200.llmops.kvcache import KVCache
     g = gen(15)

@@ -63,6 +63,9 @@ SIGNATURES: dict[str, tuple] = {
                                      _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _i64, _i32, _i64, _f32, _i32, _p]),
     "tpp_attention_decode_workspace": (_i64, [_i64, _i64, _i64, _i64]),
+    "tpp_attention_decode_qkv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _i32, _p, _p, _p,
+                                        _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64,
+                                        _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
     "tpp_attention_decode": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i64,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
     "tpp_attention_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64,

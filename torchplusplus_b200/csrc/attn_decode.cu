@@ -281,14 +281,24 @@ int64_t attn_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t 
 
 // Shared by the public entry point and by any variant that brings its own
 // workspace; `ws` must hold attn_decode_workspace_bytes(...) bytes.
+// Fused-mode inputs of tpp_attention_decode_qkv (see DecMmaArgs).
+struct FusedQkv {
+  const void* qkv; int64_t qkv_sb;
+  const void* qn_w; const void* kn_w; float eps;
+  const void* cosp; const void* sinp; int64_t cs_stride;
+  const int32_t* positions;
+};
+
 int attn_decode_run(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache,
                     const void* v_cache, int64_t c_sb, int64_t c_sh, int64_t c_ss,
                     const int32_t* seqlens, int64_t max_seqlen, void* o, int64_t o_sb,
                     int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                     int64_t window_left, float scale, void* ws, int64_t ws_bytes, int dtype,
-                    cudaStream_t st) {
+                    cudaStream_t st, const FusedQkv* fz = nullptr) {
   if (B == 0) return TPP_OK;
-  TPP_REQUIRE(q && k_cache && v_cache && o, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE((q || fz) && k_cache && v_cache && o, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(!fz || D == 64 || D == 128, TPP_ERR_UNSUPPORTED,
+              "the fused q/k norm + RoPE decode path needs head dim 64 or 128");
   TPP_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, TPP_ERR_SHAPE,
               "Hq must be a positive multiple of Hkv");
   TPP_REQUIRE(D == 64 || D == 128 || D == 256, TPP_ERR_UNSUPPORTED, "head dim must be 64, 128 or 256");
@@ -302,8 +312,16 @@ int attn_decode_run(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cac
   if (window_left >= 0 && window_left + 1 < range) range = window_left + 1;
   if (D == 64 || D == 128) {
     TPP_REQUIRE(c_ss == D, TPP_ERR_ALIGN, "cache rows must be contiguous (seq stride == head dim)");
-    DecMmaArgs m;
+    DecMmaArgs m = {};
     m.q = q; m.q_sb = q_sb; m.q_sh = q_sh;
+    if (fz) {
+      m.qkv = fz->qkv; m.qkv_sb = fz->qkv_sb;
+      m.qn_w = fz->qn_w; m.kn_w = fz->kn_w; m.eps = fz->eps;
+      m.cosp = fz->cosp; m.sinp = fz->sinp; m.cs_stride = fz->cs_stride;
+      m.positions = fz->positions;
+      m.kc = const_cast<void*>(k_cache); m.vc = const_cast<void*>(v_cache);
+      m.c_sb = c_sb; m.c_sh = c_sh; m.c_ss = c_ss;
+    }
     m.o = o; m.o_sb = o_sb; m.o_sh = o_sh;
     m.seqlens = seqlens; m.max_seqlen = max_seqlen;
     m.Hq = (int)Hq; m.Hkv = (int)Hkv; m.G = (int)(Hq / Hkv); m.passes = 1;
@@ -388,6 +406,24 @@ extern "C" int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
   return attn_decode_run(q, q_sb, q_sh, k_cache, v_cache, c_sb, c_sh, c_ss, seqlens, max_seqlen,
                          o, o_sb, o_sh, B, Hq, Hkv, D, window_left, scale, workspace,
                          workspace_bytes, dtype, as_stream(stream));
+}
+
+extern "C" int tpp_attention_decode_qkv(
+    const void* qkv, int64_t ld_qkv, const void* qn_w, const void* kn_w, float eps,
+    const void* cos, const void* sin, int64_t cs_stride, int cs_dtype,
+    const int32_t* positions, void* k_cache, void* v_cache, int64_t c_sb, int64_t c_sh,
+    int64_t c_ss, const int32_t* seqlens, int64_t max_seqlen, void* o, int64_t o_sb,
+    int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t window_left,
+    float scale, void* workspace, int64_t workspace_bytes, int dtype, void* stream) {
+  if (B == 0) return TPP_OK;
+  TPP_REQUIRE(qkv && cos && sin && positions && seqlens, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(cs_dtype == TPP_F16, TPP_ERR_DTYPE, "RoPE tables must be fp16 (compute_rope_params)");
+  TPP_REQUIRE(ld_qkv >= (Hq + 2 * Hkv) * D, TPP_ERR_SHAPE, "qkv row shorter than (Hq+2Hkv)*D");
+  TPP_REQUIRE(cs_stride >= D, TPP_ERR_SHAPE, "RoPE table row shorter than D");
+  FusedQkv fz{qkv, ld_qkv, qn_w, kn_w, eps, cos, sin, cs_stride, positions};
+  return attn_decode_run(nullptr, 0, 0, k_cache, v_cache, c_sb, c_sh, c_ss, seqlens, max_seqlen,
+                         o, o_sb, o_sh, B, Hq, Hkv, D, window_left, scale, workspace,
+                         workspace_bytes, dtype, as_stream(stream), &fz);
 }
 
 // ---------------------------------------------------------------------------

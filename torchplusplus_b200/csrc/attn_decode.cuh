@@ -18,6 +18,19 @@ struct DecMmaArgs {
   float* ws_o;     // [B, Hq, splits, D]
   float* ws_lse;   // [B, Hq, splits]
   int* err;
+  // Fused mode (qkv != nullptr): q and the step's new k/v come raw from the
+  // QKV projection row [q (Hq*D) | k (Hkv*D) | v (Hkv*D)]; the kernel applies
+  // the q/k RMSNorm (weights may be null) and RoPE at positions[b], writes
+  // the new k/v into the cache at that row and uses them directly.  Requires
+  // positions[b] == seqlens[b] - 1.
+  const void* qkv; int64_t qkv_sb;
+  const void* qn_w; const void* kn_w; float eps;
+  const void* cosp; const void* sinp; int64_t cs_stride;  // fp16 tables [ctx, D]
+  const int32_t* positions;
+  void* kc; void* vc; int64_t c_sb, c_sh, c_ss;           // cache (element strides)
+#ifdef TPP_DEBUG_STAMPS
+  unsigned dbg_id;
+#endif
 };
 
 // Split count of the tensor-core decode path for B sequences, Hq/Hkv heads

@@ -21,6 +21,7 @@
 //    splits -- write (o, lse) partials to the caller's workspace for
 //    decode_combine_kernel.
 #include <math.h>
+#include <type_traits>
 #include <cooperative_groups.h>
 #include "mma_common.cuh"
 #include "tc_common.cuh"
@@ -33,6 +34,17 @@ namespace tpp {
 
 
 namespace {
+
+#ifdef TPP_DEBUG_STAMPS
+// [launch % 32][cta < 512][16] globaltimer stamps (thread 0)
+__device__ unsigned long long g_dec_stamps[32 * 512 * 16];
+unsigned g_dec_launch = 0;
+#define DEC_TS(i) do { const unsigned _c = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
+    if (threadIdx.x == 0 && _c < 512) { unsigned long long _t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(_t)); \
+    g_dec_stamps[((p.dbg_id % 32) * 512 + _c) * 16 + (i)] = _t; } } while (0)
+#else
+#define DEC_TS(i) do {} while (0)
+#endif
 
 constexpr int kThreads = 128;
 constexpr int KT = 64;      // keys per tile
@@ -53,7 +65,10 @@ struct DecSmem {
   static constexpr uint32_t kRecv = 8 * QR * (D + 4) * 4;       // per-split (o, lse)
   static constexpr uint32_t kWork = (kRing > kWc + kRecv) ? kRing : (kWc + kRecv);
   static constexpr uint32_t kQ = QR * D * 2;
-  static constexpr size_t kBytes = 1024 + kWork + kQ + 128;
+  // + barriers (64 B), then the fused mode's new k and v rows (fp32) and the
+  // new key's score per query row
+  static constexpr uint32_t kNew = 2 * D * 4 + QR * 4;
+  static constexpr size_t kBytes = 1024 + kWork + kQ + 64 + kNew;
 };
 
 template <typename T, int D>
@@ -69,6 +84,9 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   uint8_t* sq = smem + SM::kWork;
   uint64_t* full = reinterpret_cast<uint64_t*>(sq + SM::kQ);
   uint64_t* empty = full + kStages;
+  float* knew = reinterpret_cast<float*>(sq + SM::kQ + 64);   // fused mode: new k row
+  float* vnew = knew + D;                                     //             new v row
+  float* snew = vnew + D;                                     //             q.k_new per row
   float* wc = reinterpret_cast<float*>(smem);                 // after the loop
   float* recv = reinterpret_cast<float*>(smem + SM::kWc);     // after the loop
 
@@ -80,6 +98,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   const int b = blockIdx.z;
   const int h0 = kvh * p.G + pass * QR;
   const int nh = min(QR, p.G - pass * QR);
+  DEC_TS(0);
 
   if (tid == 0) {
     prefetch_tmap(&tm_k);
@@ -91,10 +110,18 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     fence_mbar_init();
   }
   __syncthreads();
-  // Sequence lengths, the cache rows of this step and q come from earlier
-  // kernels of the step.
-  pdl_wait();
-  pdl_trigger();
+  // Unfused mode: q and this step's cache row come from the previous kernel.
+  // Fused mode: the streamed keys exclude this step's row, and the lengths
+  // and earlier rows were written by kernels of earlier steps, which had
+  // completed before this one could start (every kernel of the library calls
+  // launch_dependents only after its own wait) -- so the K/V stream starts
+  // before the wait, under the QKV projection's tail; only the raw qkv row
+  // waits for it.
+  const bool fused = p.qkv != nullptr;
+  if (!fused) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   const int64_t L = p.seqlens ? (int64_t)p.seqlens[b] : p.max_seqlen;
   int64_t lo = 0;
@@ -103,7 +130,13 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   int64_t per = (n + p.splits - 1) / p.splits;
   per = (per + KT - 1) / KT * KT;
   const int64_t k0 = lo + (int64_t)split * per;
-  const int64_t k1 = min(L, k0 + per);
+  const int64_t k1c = min(L, k0 + per);
+  // Fused mode: the CTA whose key range holds the new token's position takes
+  // that key from registers (normalised, rotated) rather than from the cache
+  // row it writes, so it streams only the keys before it.
+  const int64_t pos = fused ? (int64_t)p.positions[b] : 0;
+  const bool has_new = fused && pos >= k0 && pos < k1c;
+  const int64_t k1 = has_new ? pos : k1c;
   const int ntiles = k1 > k0 ? (int)((k1 - k0 + KT - 1) / KT) : 0;
 
   auto issue = [&](int i) {
@@ -112,26 +145,159 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     uint8_t* vd = kd + SM::kTile;
     const int key = (int)(k0 + (int64_t)i * KT);
     mbar_arrive_expect_tx(&full[s], 2 * SM::kTile);
-#pragma unroll
-    for (int bx = 0; bx < D / 64; ++bx) {
-      tma_load_4d(kd + bx * KT * 128, &tm_k, &full[s], bx * 64, key, kvh, b);
-      tma_load_4d(vd + bx * KT * 128, &tm_v, &full[s], bx * 64, key, kvh, b);
-    }
+    // one request per operand: the D/64 column boxes of the tile come from a
+    // 5-D view {64, key, D/64, kv head, batch}
+    tma_load_5d(kd, &tm_k, &full[s], 0, key, 0, kvh, b);
+    tma_load_5d(vd, &tm_v, &full[s], 0, key, 0, kvh, b);
   };
   if (tid == 0) {
     for (int i = 0; i < ntiles && i < kStages; ++i) issue(i);
   }
+  // fused mode: the static RoPE tables and norm weights load before the wait
+  constexpr int EPL = D / 32;
+  float cv[EPL], sv[EPL], wq[EPL], wk[EPL];
+  if (fused) {
+    const __half* cs = static_cast<const __half*>(p.cosp) + pos * p.cs_stride + lane * EPL;
+    const __half* sn = static_cast<const __half*>(p.sinp) + pos * p.cs_stride + lane * EPL;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      cv[j] = __half2float(cs[j]);
+      sv[j] = __half2float(sn[j]);
+      wq[j] = p.qn_w ? to_f32(static_cast<const T*>(p.qn_w)[lane * EPL + j]) : 1.f;
+      wk[j] = p.kn_w ? to_f32(static_cast<const T*>(p.kn_w)[lane * EPL + j]) : 1.f;
+    }
+    pdl_wait();
+    pdl_trigger();
+  }
+  DEC_TS(1);
 
   // ---- Q rows (heads h0 .. h0+nh-1, zero padding) -> swizzled smem -> A fragments ----
-  const T* Q = static_cast<const T*>(p.q) + b * p.q_sb;
   const uint32_t sq_a = smem_u32(sq);
-  for (int e = tid; e < QR * NCH; e += kThreads) {
-    const int r = e / NCH, ch = e % NCH;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nh) v = __ldg(reinterpret_cast<const uint4*>(Q + (int64_t)(h0 + r) * p.q_sh) + ch);
-    *reinterpret_cast<uint4*>(sq + (sw_addr(sq_a, QR, r, ch) - sq_a)) = v;
+  if (fused) {
+    // q/k RMSNorm + RoPE as qk_norm_rope_cache_kernel (rope.cu) computes them:
+    // fp32 math on the raw projection, one rounding to T at the end.  Each
+    // warp owns 4 q rows plus the new k row (every warp recomputes it, so the
+    // dot products need no block barrier); lane l holds elements
+    // [EPL*l, EPL*l + EPL), its rotate-half partner is lane l ^ 16.  All rows
+    // go through each phase together (one load round trip, interleaved
+    // shuffles).
+    constexpr int RPW = QR / 4;  // q rows per warp
+    constexpr int NRW = RPW + 1;  // + the new k row
+    using VT = typename std::conditional<EPL == 4, uint2, uint32_t>::type;
+    const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_sb;
+    VT raw[NRW], rawv = VT{};
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int r = warp + 4 * i;
+      raw[i] = r < nh ? *reinterpret_cast<const VT*>(row + (int64_t)(h0 + r) * D + lane * EPL)
+                      : VT{};
+    }
+    raw[RPW] = has_new ? *reinterpret_cast<const VT*>(row + (int64_t)(p.Hq + kvh) * D + lane * EPL)
+                       : VT{};
+    if (has_new && warp == 0)
+      rawv = *reinterpret_cast<const VT*>(row + (int64_t)(p.Hq + p.Hkv + kvh) * D + lane * EPL);
+    float x[NRW][EPL];
+#pragma unroll
+    for (int i = 0; i < NRW; ++i) {
+      const T* e = reinterpret_cast<const T*>(&raw[i]);
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) x[i][j] = to_f32(e[j]);
+    }
+    // RMSNorm (rows without a weight are left as they are)
+    float ss[NRW];
+#pragma unroll
+    for (int i = 0; i < NRW; ++i) {
+      ss[i] = 0.f;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) ss[i] += x[i][j] * x[i][j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < NRW; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+#pragma unroll
+    for (int i = 0; i < NRW; ++i) {
+      const bool has_w = i < RPW ? p.qn_w != nullptr : p.kn_w != nullptr;
+      if (!has_w) continue;
+      const float inv = rsqrtf(ss[i] / (float)D + p.eps);
+      const float* w = i < RPW ? wq : wk;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) x[i][j] *= inv * w[j];
+    }
+    // RoPE (rotate-half partner in lane ^ 16), then the one rounding to T
+    float pr[NRW][EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+#pragma unroll
+      for (int i = 0; i < NRW; ++i) pr[i][j] = __shfl_xor_sync(0xffffffffu, x[i][j], 16);
+#pragma unroll
+    for (int i = 0; i < NRW; ++i)
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const float v = lane < 16 ? x[i][j] * cv[j] - pr[i][j] * sv[j]
+                                  : x[i][j] * cv[j] + pr[i][j] * sv[j];
+        x[i][j] = to_f32(from_f32<T>(v));
+      }
+    // q rows -> swizzled smem; q . k_new per row
+    float dot[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int r = warp + 4 * i;
+      VT packed;
+      T* pe = reinterpret_cast<T*>(&packed);
+      dot[i] = 0.f;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const float v = r < nh ? x[i][j] : 0.f;
+        pe[j] = from_f32<T>(v);
+        dot[i] += v * x[RPW][j];
+      }
+      *reinterpret_cast<VT*>(sq + (sw_addr(sq_a, QR, r, (lane * EPL) >> 3) - sq_a) +
+                             ((lane * EPL) & 7) * 2) = packed;
+    }
+    if (has_new) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) dot[i] += __shfl_xor_sync(0xffffffffu, dot[i], o);
+      if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+          const int r = warp + 4 * i;
+          snew[r] = r < nh ? dot[i] * p.scale_log2 : -INFINITY;
+        }
+      }
+      if (warp == 0) {
+        // the step's cache rows (k normed + rotated, v as projected) and the
+        // v row the fold below reads
+        VT pk, pv;
+        T* ek = reinterpret_cast<T*>(&pk);
+        T* ev = reinterpret_cast<T*>(&pv);
+        const T* rv = reinterpret_cast<const T*>(&rawv);
+#pragma unroll
+        for (int j = 0; j < EPL; ++j) {
+          ek[j] = from_f32<T>(x[RPW][j]);
+          ev[j] = rv[j];
+          vnew[lane * EPL + j] = to_f32(rv[j]);
+        }
+        if (pass == 0) {
+          const int64_t off = b * p.c_sb + kvh * p.c_sh + pos * p.c_ss + lane * EPL;
+          *reinterpret_cast<VT*>(static_cast<T*>(p.kc) + off) = pk;
+          *reinterpret_cast<VT*>(static_cast<T*>(p.vc) + off) = pv;
+        }
+      }
+    }
+  } else {
+    const T* Q = static_cast<const T*>(p.q) + b * p.q_sb;
+    for (int e = tid; e < QR * NCH; e += kThreads) {
+      const int r = e / NCH, ch = e % NCH;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < nh) v = __ldg(reinterpret_cast<const uint4*>(Q + (int64_t)(h0 + r) * p.q_sh) + ch);
+      *reinterpret_cast<uint4*>(sq + (sw_addr(sq_a, QR, r, ch) - sq_a)) = v;
+    }
   }
   __syncthreads();
+  DEC_TS(2);
   uint32_t qf[D / 16][4];
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
@@ -154,21 +320,31 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
       if (ok) issue(i - 1 + kStages);
     }
     if (!mbar_wait(&full[s], (i / kStages) & 1, p.err, 22)) { ok = false; break; }
+    if (i < 10) DEC_TS(3 + i);
     const uint32_t kb = smem_u32(ring + s * 2 * SM::kTile);
     const uint32_t vb = kb + SM::kTile;
     const int kr0 = warp * 16;  // this warp's 16 keys of the tile
 
-    float sc[2][4];
+    // S = Q.K^T for this warp's 16 keys; even and odd k-steps accumulate in
+    // separate registers (4 independent MMA chains instead of 2)
+    float sc[2][4], sd[2][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[j][e] = sd[j][e] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
       uint32_t bf[4];
       const int r = kr0 + (lane & 7) + (lane >> 4) * 8;
       ldsm_x4(sw_addr(kb, KT, r, ks * 2 + ((lane >> 3) & 1)), bf);
-      mma<T>(sc[0], qf[ks], bf[0], bf[1]);
-      mma<T>(sc[1], qf[ks], bf[2], bf[3]);
+      float (&acc)[2][4] = (ks & 1) ? sd : sc;
+      mma<T>(acc[0], qf[ks], bf[0], bf[1]);
+      mma<T>(acc[1], qf[ks], bf[2], bf[3]);
     }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[j][e] += sd[j][e];
     const int64_t kbase = k0 + (int64_t)i * KT + kr0;
 #pragma unroll
     for (int j = 0; j < 2; ++j)
@@ -220,6 +396,27 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     if (lane == 0) mbar_arrive(&empty[s]);
   }
 
+  DEC_TS(13);
+  // ---- fused mode: fold the new key into warp 0's online-softmax state ----
+  if (has_new && warp == 0) {
+    __syncwarp();
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const float sk = snew[g + hr * 8];
+      if (sk == -INFINITY) continue;  // padding row
+      const float mx = fmaxf(m_r[hr], sk);
+      const float corr = exp2f(m_r[hr] - mx);  // 0 when no key was seen yet
+      const float pn = exp2f(sk - mx);
+      l_r[hr] = l_r[hr] * corr + (c == 0 ? pn : 0.f);  // l is summed over the quad
+#pragma unroll
+      for (int d = 0; d < D / 8; ++d) {
+        o[d][2 * hr] = o[d][2 * hr] * corr + pn * vnew[d * 8 + 2 * c];
+        o[d][2 * hr + 1] = o[d][2 * hr + 1] * corr + pn * vnew[d * 8 + 2 * c + 1];
+      }
+      m_r[hr] = mx;
+    }
+  }
+
   // ---- merge the 4 warps (rows g, g+8 of each; l is quad-partial) ----
   if (p.cluster && p.splits > 1)
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -243,34 +440,46 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   // receive slot of this split (cluster mode: slots 0..7 = cluster ranks;
   // otherwise slot 0)
   const int slot = (p.cluster && p.splits > 1) ? split : 0;
-  for (int e = tid; e < nh * D; e += kThreads) {
-    const int r = e / D, d = e % D;
+  // per row: the weight of each warp's partial (exp2(m_w - M) / L) and lse,
+  // computed once (into the spent new-key area), then applied per element
+  float* fac = knew;           // [QR][4]
+  float* rlse = knew + 4 * QR; // [QR]
+  if (tid < nh) {
+    const int r = tid;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 4; ++w) M = fmaxf(M, wc[(w * QR + r) * (D + 2)]);
-    float Ls = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+    float e[4], Ls = 0.f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float* bw = wc + (w * QR + r) * (D + 2);
-        const float sc = bw[0] == -INFINITY ? 0.f : exp2f(bw[0] - M);
-        Ls += bw[1] * sc;
-        O += bw[2 + d] * sc;
-      }
+    for (int w = 0; w < 4; ++w) {
+      const float* bw = wc + (w * QR + r) * (D + 2);
+      e[w] = (M == -INFINITY || bw[0] == -INFINITY) ? 0.f : exp2f(bw[0] - M);
+      Ls += bw[1] * e[w];
     }
-    const float on = Ls > 0.f ? O / Ls : 0.f;
-    const float lse = Ls > 0.f ? M + log2f(Ls) : -INFINITY;
+    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) fac[r * 4 + w] = e[w] * inv;
+    rlse[r] = Ls > 0.f ? M + log2f(Ls) : -INFINITY;
+  }
+  __syncthreads();
+  for (int e = tid; e < nh * D; e += kThreads) {
+    const int r = e / D, d = e % D;
+    float on = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) on += wc[(w * QR + r) * (D + 2) + 2 + d] * fac[r * 4 + w];
     recv[(slot * QR + r) * (D + 4) + 4 + d] = on;
-    if (d == 0) recv[(slot * QR + r) * (D + 4)] = lse;
+    if (d == 0) recv[(slot * QR + r) * (D + 4)] = rlse[r];
   }
   __syncthreads();
 
   if (p.splits == 1) {
+    DEC_TS(14);
     T* out = static_cast<T*>(p.o) + b * p.o_sb;
     for (int e = tid; e < nh * D; e += kThreads) {
       const int r = e / D, d = e % D;
       out[(int64_t)(h0 + r) * p.o_sh + d] = from_f32<T>(recv[r * (D + 4) + 4 + d]);
     }
+    DEC_TS(15);
     return;
   }
   if (!p.cluster) {
@@ -333,17 +542,29 @@ int decode_mma_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t range) {
   return (int)(s < 1 ? 1 : s);
 }
 
+#ifdef TPP_DEBUG_STAMPS
+extern "C" void tpp_debug_dec_stamps(unsigned long long* host) {
+  cudaMemcpyFromSymbol(host, g_dec_stamps, sizeof(unsigned long long) * 32 * 512 * 16);
+}
+extern "C" unsigned tpp_debug_dec_launches() { return g_dec_launch; }
+#endif
+
 int decode_mma_launch(DecMmaArgs& a, const void* k_cache, const void* v_cache, int64_t c_sb,
                       int64_t c_sh, int64_t c_ss, int64_t B, int64_t D, int dtype,
                       cudaStream_t st) {
+#ifdef TPP_DEBUG_STAMPS
+  a.dbg_id = g_dec_launch++;
+#endif
   CUtensorMap tk, tv;
   const uint64_t smax = (uint64_t)(a.max_seqlen > 0 ? a.max_seqlen : 1);
-  const uint64_t dims[4] = {(uint64_t)D, smax, (uint64_t)a.Hkv, (uint64_t)B};
-  const uint64_t strides[3] = {(uint64_t)c_ss * 2, (uint64_t)c_sh * 2, (uint64_t)c_sb * 2};
-  const uint32_t box[4] = {64, KT, 1, 1};
-  int rc = make_tmap(&tk, k_cache, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  // {64 columns, key, column box (D/64), kv head, batch}: the tile's column
+  // boxes land one after another ([box][key][128 B]), as the kernel reads them
+  const uint64_t dims[5] = {64, smax, (uint64_t)(D / 64), (uint64_t)a.Hkv, (uint64_t)B};
+  const uint64_t strides[4] = {(uint64_t)c_ss * 2, 128, (uint64_t)c_sh * 2, (uint64_t)c_sb * 2};
+  const uint32_t box[5] = {64, KT, (uint32_t)(D / 64), 1, 1};
+  int rc = make_tmap(&tk, k_cache, dtype, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TPP_OK) return rc;
-  rc = make_tmap(&tv, v_cache, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = make_tmap(&tv, v_cache, dtype, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TPP_OK) return rc;
   a.passes = (a.G + QR - 1) / QR;
   a.cluster = a.splits <= 8 ? 1 : 0;

@@ -547,10 +547,14 @@ extern "C" unsigned tpp_debug_xs_launches() { return g_xs_launch; }
 // rows) for an N-wide layer on this device, or 0 when N is too wide.
 int xs_outputs_per_cta(int64_t N, int act) {
   const int sms = num_sms();
+  const int per_row = act == TPP_ACT_SWIGLU ? 2 : 1;  // weight rows per output
   int64_t nro = (N + sms - 1) / sms;
   nro = (nro + 7) / 8 * 8;
-  const int64_t nr = act == TPP_ACT_SWIGLU ? 2 * nro : nro;
-  return nr > 8 * kMaxNT ? 0 : (int)nro;
+  // Prefer slices of <= 32 weight rows (4 n-tiles: two CTAs fit an SM) as
+  // long as the grid still fits two CTAs per SM.
+  const int64_t small = 32 / per_row;
+  if (nro * per_row > 32 && (N + small - 1) / small <= 2 * (int64_t)sms) nro = small;
+  return nro * per_row > 8 * kMaxNT ? 0 : (int)nro;
 }
 int xs_token_tile(int64_t M) { return M <= 16 ? 16 : 32; }
 

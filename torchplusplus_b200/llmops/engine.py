@@ -2,11 +2,12 @@
 CUDA graph of sm_100a kernels, with every buffer static and the sampled token
 fed back on the device.
 
-Per step and layer (6 kernels): RMSNorm+QKV linear (norm fused into the
-GEMM) -> fused q/k-norm + RoPE + KV write -> tensor-core decode attention
-(split-KV merged in a cluster) -> o-proj linear with the residual add in its
-epilogue -> RMSNorm+gate/up linear with the SwiGLU product in its epilogue ->
-down linear with the residual add in its epilogue.  Then RMSNorm+LM-head
+Per step and layer (5 kernels): RMSNorm+QKV linear (norm fused into the
+GEMM) -> decode attention with the q/k norm, RoPE and KV-cache write of the
+new token fused in (split-KV merged in a cluster) -> o-proj linear with the
+residual add in its epilogue -> RMSNorm+gate/up linear with the SwiGLU
+product in its epilogue -> down linear with the residual add in its
+epilogue.  Then RMSNorm+LM-head
 linear -> argmax -> decode_advance (token history, positions).  Nothing
 returns to the host between steps.
 
@@ -83,6 +84,9 @@ class DecodeEngine:
         self.logits = z(B, cfg.vocab_size)
         nws = ops.decode_workspace_bytes(B, self.Hq, max_seq_len, self.D)
         self.ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+        # q/k norm + RoPE + KV append inside the decode-attention launch (head
+        # dims 64 / 128 with fp16 RoPE tables); otherwise a separate kernel.
+        self.fuse_qk_attention = self.D in (64, 128) and self.cos.dtype == torch.float16
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step: int | None = None
         self.prompt_len = 0
@@ -93,10 +97,18 @@ class DecodeEngine:
         ops.embedding(self.tokens, self.emb, out=self.x)
         for L, c in zip(self.layers, self.caches):
             ops.rmsnorm_linear(self.x, L["wqkv_f"], self.eps, out=self.qkv.view(B, -1))
-            ops.qk_norm_rope_cache(self.qkv, L["qn"], L["kn"], self.eps, self.cos, self.sin,
-                                   self.positions, c.k_cache, c.v_cache, Hq, Hkv, q_out=self.q)
-            ops.attention_decode(self.q.view(B, Hq, D), c.k_cache, c.v_cache, self.seqlens,
-                                 self.max_seq_len, out=self.o, workspace=self.ws)
+            if self.fuse_qk_attention:
+                ops.attention_decode_qkv(self.qkv, L["qn"], L["kn"], self.eps, self.cos,
+                                         self.sin, self.positions, c.k_cache, c.v_cache,
+                                         self.seqlens, self.max_seq_len, Hq, Hkv, out=self.o,
+                                         workspace=self.ws)
+            else:
+                ops.qk_norm_rope_cache(self.qkv, L["qn"], L["kn"], self.eps, self.cos,
+                                       self.sin, self.positions, c.k_cache, c.v_cache, Hq, Hkv,
+                                       q_out=self.q)
+                ops.attention_decode(self.q.view(B, Hq, D), c.k_cache, c.v_cache,
+                                     self.seqlens, self.max_seq_len, out=self.o,
+                                     workspace=self.ws)
             ops.linear(self.o.view(B, Hq * D), L["wo"], residual=self.x, out=self.x)
             ops.rmsnorm_linear(self.x, L["wgu_f"], self.eps, act="swiglu", out=self.ff)
             ops.linear(self.ff, L["wdown"], residual=self.x, out=self.x)

@@ -360,6 +360,48 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
+def attention_decode_qkv(qkv: torch.Tensor, q_norm_w: torch.Tensor | None,
+                         k_norm_w: torch.Tensor | None, eps: float, cos: torch.Tensor,
+                         sin: torch.Tensor, positions: torch.Tensor, k_cache: torch.Tensor,
+                         v_cache: torch.Tensor, seqlens: torch.Tensor, max_seqlen: int,
+                         Hq: int, Hkv: int, window_left: int = -1, scale: float | None = None,
+                         out: torch.Tensor | None = None,
+                         workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode step in one launch: qkv [B, 1, (Hq+2Hkv)*D] raw projection rows ->
+    q/k RMSNorm + RoPE at positions[b], new k/v written into the caches at row
+    positions[b], attention over keys up to it -> o [B, Hq, D].  Requires
+    positions == seqlens - 1 (int32 [B] each); fp16 RoPE tables."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, positions, k_cache, v_cache, seqlens)
+    dt = _half(qkv, "qkv")
+    _same_dtype(qkv, k_cache, v_cache, q_norm_w, k_norm_w)
+    B = qkv.shape[0]
+    D = k_cache.shape[-1]
+    if qkv.shape[-1] != (Hq + 2 * Hkv) * D or qkv.stride(-1) != 1:
+        raise ValueError("qkv must be [B, 1, (Hq+2Hkv)*D]")
+    if k_cache.shape[:2] != (B, Hkv) or v_cache.shape != k_cache.shape \
+            or k_cache.stride() != v_cache.stride():
+        raise ValueError("caches must be [B, Hkv, Smax, D] with identical layouts")
+    for t, nm in ((positions, "positions"), (seqlens, "seqlens")):
+        if t.dtype != torch.int32 or t.numel() != B:
+            raise ValueError(f"{nm} must be int32 [B]")
+    cos, sin, cs_stride, cs_dt = _table(cos, sin, D)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=qkv.dtype, device=qkv.device)
+    need = decode_workspace_bytes(B, Hq, max_seqlen, D)
+    if workspace is None and need > 0:
+        workspace = torch.empty(need, dtype=torch.uint8, device=qkv.device)
+    N.call("tpp_attention_decode_qkv", qkv.data_ptr(), qkv.stride(0), N.ptr(q_norm_w),
+           N.ptr(k_norm_w), float(eps), cos.data_ptr(), sin.data_ptr(), cs_stride, cs_dt,
+           positions.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+           k_cache.stride(1), k_cache.stride(2), seqlens.data_ptr(), int(max_seqlen),
+           out.data_ptr(), out.stride(0), out.stride(1), B, Hq, Hkv, D, int(window_left),
+           float(scale), N.ptr(workspace), 0 if workspace is None else workspace.numel(), dt,
+           N.stream_of(qkv))
+    return out
+
+
 # ---------------------------------------------------------------- cache / step helpers
 def qk_norm_rope_cache(qkv: torch.Tensor, q_norm_w: torch.Tensor | None,
                        k_norm_w: torch.Tensor | None, eps: float, cos: torch.Tensor,
