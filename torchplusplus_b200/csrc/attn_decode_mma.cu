@@ -61,7 +61,7 @@ template <int D>
 struct DecSmem {
   static constexpr uint32_t kTile = KT * D * 2;                 // one K or V tile
   static constexpr uint32_t kRing = kStages * 2 * kTile;
-  static constexpr uint32_t kWc = 4 * QR * (D + 2) * 4;         // per-warp (m, l, o)
+  static constexpr uint32_t kWc = 4 * QR * (D + 4) * 4;         // per-warp (m, l, -, -, o)
   static constexpr uint32_t kRecv = 8 * QR * (D + 4) * 4;       // per-split (o, lse)
   static constexpr uint32_t kWork = (kRing > kWc + kRecv) ? kRing : (kWc + kRecv);
   static constexpr uint32_t kQ = QR * D * 2;
@@ -311,23 +311,12 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
   bool ok = true;
 
-  for (int i = 0; i < ntiles; ++i) {
-    const int s = i % kStages;
-    // refill the stage released one iteration ago
-    if (tid == 0 && i >= 1 && i - 1 + kStages < ntiles) {
-      const int sp = (i - 1) % kStages;
-      ok = mbar_wait(&empty[sp], ((i - 1) / kStages) & 1, p.err, 21) && ok;
-      if (ok) issue(i - 1 + kStages);
-    }
-    if (!mbar_wait(&full[s], (i / kStages) & 1, p.err, 22)) { ok = false; break; }
-    if (i < 10) DEC_TS(3 + i);
-    const uint32_t kb = smem_u32(ring + s * 2 * SM::kTile);
-    const uint32_t vb = kb + SM::kTile;
-    const int kr0 = warp * 16;  // this warp's 16 keys of the tile
-
-    // S = Q.K^T for this warp's 16 keys; even and odd k-steps accumulate in
-    // separate registers (4 independent MMA chains instead of 2)
-    float sc[2][4], sd[2][4];
+  const int kr0 = warp * 16;  // this warp's 16 keys of every tile
+  // S = Q.K^T for this warp's 16 keys of tile i; even and odd k-steps
+  // accumulate in separate registers (4 independent MMA chains instead of 2)
+  auto compute_s = [&](int i, float (&sc)[2][4]) {
+    const uint32_t kb = smem_u32(ring + (i % kStages) * 2 * SM::kTile);
+    float sd[2][4];
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -345,6 +334,24 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) sc[j][e] += sd[j][e];
+  };
+  // Software pipeline: the S MMAs of tile i+1 are issued before the PV MMAs
+  // of tile i (they are independent), so the two latency chains overlap.
+  float sc[2][4];
+  if (ntiles > 0) {
+    if (mbar_wait(&full[0], 0, p.err, 22)) compute_s(0, sc);
+    else ok = false;
+  }
+  for (int i = 0; i < ntiles && ok; ++i) {
+    const int s = i % kStages;
+    // refill the stage released one iteration ago
+    if (tid == 0 && i >= 1 && i - 1 + kStages < ntiles) {
+      const int sp = (i - 1) % kStages;
+      ok = mbar_wait(&empty[sp], ((i - 1) / kStages) & 1, p.err, 21) && ok;
+      if (ok) issue(i - 1 + kStages);
+    }
+    if (i < 10) DEC_TS(3 + i);
+    const uint32_t vb = smem_u32(ring + s * 2 * SM::kTile) + SM::kTile;
     const int64_t kbase = k0 + (int64_t)i * KT + kr0;
 #pragma unroll
     for (int j = 0; j < 2; ++j)
@@ -384,6 +391,13 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     pa[1] = pack2<T>(sc[0][2], sc[0][3]);
     pa[2] = pack2<T>(sc[1][0], sc[1][1]);
     pa[3] = pack2<T>(sc[1][2], sc[1][3]);
+    const bool more = i + 1 < ntiles;
+    if (more) {
+      if (mbar_wait(&full[(i + 1) % kStages], ((i + 1) / kStages) & 1, p.err, 22))
+        compute_s(i + 1, sc);  // sc is free again: P went to registers above
+      else
+        ok = false;
+    }
 #pragma unroll
     for (int dp = 0; dp < D / 16; ++dp) {
       uint32_t bf[4];
@@ -427,15 +441,57 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
     const int r = g + hr * 8;
-    float* base = wc + (warp * QR + r) * (D + 2);
+    float* base = wc + (warp * QR + r) * (D + 4);
     if (c == 0) { base[0] = m_r[hr]; base[1] = l; }
 #pragma unroll
-    for (int d = 0; d < D / 8; ++d) {
-      base[2 + d * 8 + 2 * c] = o[d][2 * hr];
-      base[2 + d * 8 + 2 * c + 1] = o[d][2 * hr + 1];
-    }
+    for (int d = 0; d < D / 8; ++d)
+      *reinterpret_cast<float2*>(base + 4 + d * 8 + 2 * c) = make_float2(o[d][2 * hr], o[d][2 * hr + 1]);
   }
   __syncthreads();
+  if (p.splits == 1) {
+    // One split: each thread finishes 8 consecutive outputs of a row straight
+    // from the four warps' partials (weights exp2(m_w - M) / L recomputed per
+    // item) and stores them with one 16-byte write.
+    DEC_TS(14);
+    T* out = static_cast<T*>(p.o) + b * p.o_sb;
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.o) & 15) == 0) && (p.o_sh % 8 == 0) &&
+                     (p.o_sb % 8 == 0);
+    for (int e = tid; e < nh * (D / 8); e += kThreads) {
+      const int r = e / (D / 8), d0 = (e % (D / 8)) * 8;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) M = fmaxf(M, wc[(w * QR + r) * (D + 4)]);
+      float ew[4], Ls = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float* bw = wc + (w * QR + r) * (D + 4);
+        ew[w] = (M == -INFINITY || bw[0] == -INFINITY) ? 0.f : exp2f(bw[0] - M);
+        Ls += bw[1] * ew[w];
+      }
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+      float acc[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float* ow = wc + (w * QR + r) * (D + 4) + 4 + d0;
+        const float4 a0 = *reinterpret_cast<const float4*>(ow);
+        const float4 a1 = *reinterpret_cast<const float4*>(ow + 4);
+        const float f = ew[w] * inv;
+        acc[0] += a0.x * f; acc[1] += a0.y * f; acc[2] += a0.z * f; acc[3] += a0.w * f;
+        acc[4] += a1.x * f; acc[5] += a1.y * f; acc[6] += a1.z * f; acc[7] += a1.w * f;
+      }
+      T* dst = out + (int64_t)(h0 + r) * p.o_sh + d0;
+      if (vec) {
+        *reinterpret_cast<uint4*>(dst) = pack8<T>(acc);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = from_f32<T>(acc[q]);
+      }
+    }
+    DEC_TS(15);
+    return;
+  }
   // CTA partial for row r: normalised o (fp32) and lse (log2 domain) in the
   // receive slot of this split (cluster mode: slots 0..7 = cluster ranks;
   // otherwise slot 0)
@@ -448,11 +504,11 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const int r = tid;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, wc[(w * QR + r) * (D + 2)]);
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wc[(w * QR + r) * (D + 4)]);
     float e[4], Ls = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float* bw = wc + (w * QR + r) * (D + 2);
+      const float* bw = wc + (w * QR + r) * (D + 4);
       e[w] = (M == -INFINITY || bw[0] == -INFINITY) ? 0.f : exp2f(bw[0] - M);
       Ls += bw[1] * e[w];
     }
@@ -466,22 +522,13 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const int r = e / D, d = e % D;
     float on = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) on += wc[(w * QR + r) * (D + 2) + 2 + d] * fac[r * 4 + w];
+    for (int w = 0; w < 4; ++w) on += wc[(w * QR + r) * (D + 4) + 4 + d] * fac[r * 4 + w];
     recv[(slot * QR + r) * (D + 4) + 4 + d] = on;
     if (d == 0) recv[(slot * QR + r) * (D + 4)] = rlse[r];
   }
   __syncthreads();
 
-  if (p.splits == 1) {
-    DEC_TS(14);
-    T* out = static_cast<T*>(p.o) + b * p.o_sb;
-    for (int e = tid; e < nh * D; e += kThreads) {
-      const int r = e / D, d = e % D;
-      out[(int64_t)(h0 + r) * p.o_sh + d] = from_f32<T>(recv[r * (D + 4) + 4 + d]);
-    }
-    DEC_TS(15);
-    return;
-  }
+
   if (!p.cluster) {
     for (int e = tid; e < nh * D; e += kThreads) {
       const int r = e / D, d = e % D;
