@@ -165,19 +165,20 @@ def run_reference(args, rank, world):
 
 # ---------------------------------------------------------------- GPU arm
 def linear_roofline(eng, reps: int = 20) -> dict:
-    """Times the decode linear kernel alone: all 4*L + 1 linear launches of one
-    decode step captured in a graph and replayed; algorithmic bytes = weights
-    + x + y (+ residual) per launch."""
+    """Times the decode linear kernels alone: all (4*L + 1) x lanes linear
+    launches of one decode step captured in a graph (one stream) and replayed;
+    algorithmic bytes = weights + x + y (+ residual) per launch."""
     from torchplusplus_b200 import ops
-    B = eng.batch_size
     byts = 0
     calls = []
-    for L in eng.layers:
-        calls += [(eng.x, L["wqkv_f"], "none", None, eng.qkv.view(B, -1), True),
-                  (eng.o.view(B, -1), L["wo"], "none", eng.x, eng.x, False),
-                  (eng.x, L["wgu_f"], "swiglu", None, eng.ff, True),
-                  (eng.ff, L["wdown"], "none", eng.x, eng.x, False)]
-    calls.append((eng.x, eng.lm_head_f, "none", None, eng.logits, True))
+    for ln in eng.lanes:  # each lane (sub-batch) reads every weight once
+        n, x = ln["n"], ln["x"]
+        for L in eng.layers:
+            calls += [(x, L["wqkv_f"], "none", None, ln["qkv"].view(n, -1), True),
+                      (ln["o"].view(n, -1), L["wo"], "none", x, x, False),
+                      (x, L["wgu_f"], "swiglu", None, ln["ff"], True),
+                      (ln["ff"], L["wdown"], "none", x, x, False)]
+        calls.append((x, eng.lm_head_f, "none", None, ln["logits"], True))
     for x, w, act, r, y, nrm in calls:
         byts += w.numel() * 2 + x.numel() * 2 + y.numel() * 2 * (2 if r is not None else 1)
     s = torch.cuda.Stream()

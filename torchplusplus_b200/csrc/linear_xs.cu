@@ -554,6 +554,12 @@ int xs_outputs_per_cta(int64_t N, int act) {
   // long as the grid still fits two CTAs per SM.
   const int64_t small = 32 / per_row;
   if (nro * per_row > 32 && (N + small - 1) / small <= 2 * (int64_t)sms) nro = small;
+#ifdef TPP_DEBUG_STAMPS
+  if (const char* e = getenv("TPP_XS_ROWS")) {  // tuning experiments only
+    const int64_t f = atoi(e) / per_row;
+    if (f >= 8 && f % 8 == 0) nro = f;
+  }
+#endif
   return nro * per_row > 8 * kMaxNT ? 0 : (int)nro;
 }
 int xs_token_tile(int64_t M) { return M <= 16 ? 16 : 32; }

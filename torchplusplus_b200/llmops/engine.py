@@ -24,12 +24,17 @@ import torch
 
 from .. import _native as N
 from .. import ops
+from ..replicas import shard
 from .kvcache import KVCache
 
 
 class DecodeEngine:
+    """`lanes` > 1 splits the batch into that many independent sub-batches
+    whose decode steps are recorded as parallel branches of the one CUDA
+    graph (each weight is then read once per lane); the default is one lane
+    (see the measurement noted below)."""
 
-    def __init__(self, model, batch_size: int, max_seq_len: int):
+    def __init__(self, model, batch_size: int, max_seq_len: int, lanes: int | None = None):
         cfg = model.cfg
         dev = model.out_head.weight.device
         self.model = model
@@ -76,14 +81,27 @@ class DecodeEngine:
         self.positions = z(B, d=torch.int32)
         self.seqlens = z(B, d=torch.int32)
         self.out_ids = z(B, max_seq_len, d=torch.int64)
-        self.x, self.h = z(B, E), z(B, E)
-        self.qkv = z(B, 1, W)
-        self.q = z(B, 1, self.Hq, self.D)
-        self.o = z(B, self.Hq, self.D)
-        self.ff = z(B, cfg.hidden_dim)
         self.logits = z(B, cfg.vocab_size)
-        nws = ops.decode_workspace_bytes(B, self.Hq, max_seq_len, self.D)
-        self.ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+        if lanes is None:
+            # measured on B200 (Qwen3-0.6B shape, 32 sequences): one lane 1265 us
+            # a step, two lanes of 16 1313 us (the branches overlap only ~40%:
+            # each lane's kernels plus their early-starting successors do not
+            # all fit the SMs), so one lane unless asked
+            lanes = 1
+        self.lanes = []
+        for i in range(max(1, min(lanes, B))):
+            b0, n = shard(B, i, max(1, min(lanes, B)))
+            sl = slice(b0, b0 + n)
+            nws = ops.decode_workspace_bytes(n, self.Hq, max_seq_len, self.D)
+            self.lanes.append(dict(
+                b=sl, n=n,
+                tokens=self.tokens[sl], positions=self.positions[sl],
+                seqlens=self.seqlens[sl], out_ids=self.out_ids[sl],
+                logits=self.logits[sl],
+                x=z(n, E), qkv=z(n, 1, W), q=z(n, 1, self.Hq, self.D),
+                o=z(n, self.Hq, self.D), ff=z(n, cfg.hidden_dim),
+                ws=torch.empty(max(nws, 16), dtype=torch.uint8, device=dev),
+                k=[c.k_cache[sl] for c in self.caches], v=[c.v_cache[sl] for c in self.caches]))
         # q/k norm + RoPE + KV append inside the decode-attention launch (head
         # dims 64 / 128 with fp16 RoPE tables); otherwise a separate kernel.
         self.fuse_qk_attention = self.D in (64, 128) and self.cos.dtype == torch.float16
@@ -92,29 +110,33 @@ class DecodeEngine:
         self.prompt_len = 0
 
     # ------------------------------------------------------------ one step
-    def _step(self) -> None:
-        B, Hq, Hkv, D = self.batch_size, self.Hq, self.Hkv, self.D
-        ops.embedding(self.tokens, self.emb, out=self.x)
-        for L, c in zip(self.layers, self.caches):
-            ops.rmsnorm_linear(self.x, L["wqkv_f"], self.eps, out=self.qkv.view(B, -1))
+    def _step_lane(self, ln: dict) -> None:
+        n, Hq, Hkv, D = ln["n"], self.Hq, self.Hkv, self.D
+        x = ln["x"]
+        ops.embedding(ln["tokens"], self.emb, out=x)
+        for L, kc, vc in zip(self.layers, ln["k"], ln["v"]):
+            ops.rmsnorm_linear(x, L["wqkv_f"], self.eps, out=ln["qkv"].view(n, -1))
             if self.fuse_qk_attention:
-                ops.attention_decode_qkv(self.qkv, L["qn"], L["kn"], self.eps, self.cos,
-                                         self.sin, self.positions, c.k_cache, c.v_cache,
-                                         self.seqlens, self.max_seq_len, Hq, Hkv, out=self.o,
-                                         workspace=self.ws)
+                ops.attention_decode_qkv(ln["qkv"], L["qn"], L["kn"], self.eps, self.cos,
+                                         self.sin, ln["positions"], kc, vc, ln["seqlens"],
+                                         self.max_seq_len, Hq, Hkv, out=ln["o"],
+                                         workspace=ln["ws"])
             else:
-                ops.qk_norm_rope_cache(self.qkv, L["qn"], L["kn"], self.eps, self.cos,
-                                       self.sin, self.positions, c.k_cache, c.v_cache, Hq, Hkv,
-                                       q_out=self.q)
-                ops.attention_decode(self.q.view(B, Hq, D), c.k_cache, c.v_cache,
-                                     self.seqlens, self.max_seq_len, out=self.o,
-                                     workspace=self.ws)
-            ops.linear(self.o.view(B, Hq * D), L["wo"], residual=self.x, out=self.x)
-            ops.rmsnorm_linear(self.x, L["wgu_f"], self.eps, act="swiglu", out=self.ff)
-            ops.linear(self.ff, L["wdown"], residual=self.x, out=self.x)
-        ops.rmsnorm_linear(self.x, self.lm_head_f, self.eps, out=self.logits)
-        ops.argmax(self.logits, out=self.tokens)
-        ops.decode_advance(self.tokens, self.out_ids, self.positions, self.seqlens)
+                ops.qk_norm_rope_cache(ln["qkv"], L["qn"], L["kn"], self.eps, self.cos,
+                                       self.sin, ln["positions"], kc, vc, Hq, Hkv,
+                                       q_out=ln["q"])
+                ops.attention_decode(ln["q"].view(n, Hq, D), kc, vc, ln["seqlens"],
+                                     self.max_seq_len, out=ln["o"], workspace=ln["ws"])
+            ops.linear(ln["o"].view(n, Hq * D), L["wo"], residual=x, out=x)
+            ops.rmsnorm_linear(x, L["wgu_f"], self.eps, act="swiglu", out=ln["ff"])
+            ops.linear(ln["ff"], L["wdown"], residual=x, out=x)
+        ops.rmsnorm_linear(x, self.lm_head_f, self.eps, out=ln["logits"])
+        ops.argmax(ln["logits"], out=ln["tokens"])
+        ops.decode_advance(ln["tokens"], ln["out_ids"], ln["positions"], ln["seqlens"])
+
+    def _step(self) -> None:
+        for ln in self.lanes:
+            self._step_lane(ln)
 
     def step_eager(self) -> None:
         """One decode step launched directly (no graph); used by tests."""
@@ -122,16 +144,27 @@ class DecodeEngine:
 
     def capture(self) -> None:
         """Records one decode step into a CUDA graph (the capture does not
-        execute it)."""
-        s = torch.cuda.Stream(self.device)
-        s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
+        execute it); with several lanes each lane is a parallel branch."""
+        main = torch.cuda.Stream(self.device)
+        main.wait_stream(torch.cuda.current_stream(self.device))
+        side = [torch.cuda.Stream(self.device) for _ in self.lanes]
+        with torch.cuda.stream(main):
             n0 = N.launch_count()
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=s):
-                self._step()
+            with torch.cuda.graph(g, stream=main):
+                if len(self.lanes) == 1:
+                    self._step_lane(self.lanes[0])
+                else:
+                    fork = torch.cuda.Event()
+                    fork.record(main)
+                    for s, ln in zip(side, self.lanes):
+                        s.wait_event(fork)
+                        with torch.cuda.stream(s):
+                            self._step_lane(ln)
+                    for s in side:
+                        main.wait_stream(s)
             self.launches_per_step = N.launch_count() - n0
-        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.current_stream(self.device).wait_stream(main)
         self.graph = g
 
     # ------------------------------------------------------------ prefill
