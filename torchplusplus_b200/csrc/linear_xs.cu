@@ -48,6 +48,7 @@ constexpr int kMaxNT = 8;                      // 8-row n-tiles per CTA (NR <= 6
 // prefetch its weights) while this one finishes.
 constexpr int kMaxStages = 4;
 constexpr size_t kBudget = 110 * 1024;  // two CTAs (of two kernels) per SM
+constexpr size_t kBudget16 = 72 * 1024; // 16-token tiles: three CTAs per SM
 
 struct XsArgs {
   const void* bias;
@@ -109,7 +110,7 @@ __device__ __forceinline__ float sq2(uint32_t v) {
 }
 
 template <typename T, int BN, int NTM, bool SWIGLU, bool NORM>
-__global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
     linear_xs_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_x, XsArgs p) {
   constexpr int MT = BN / 16;  // m-tiles (16 tokens)
@@ -132,8 +133,9 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * NRO;  // first output (and weight row) of this CTA
+  const int t0 = blockIdx.y * BN;     // first token of this CTA (token-split grids)
   const int nkb = (p.K + 63) / 64;
-  const int mt = p.M < BN ? p.M : BN;
+  const int mt = p.M - t0 < BN ? p.M - t0 : BN;
 
 #ifdef TPP_DEBUG_STAMPS
   const unsigned long long clk0 = clock64();
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
         bulk_load(dst, p.xpk + (size_t)c * KC * BN * 128, (uint32_t)kbc(c) * BN * 128,
                   &full[c % S]);
       else
-        tma_load_3d(dst, &tm_x, &full[c % S], 0, 0, c * KC);
+        tma_load_3d(dst, &tm_x, &full[c % S], 0, t0, c * KC);
     };
     XS_TS(4);
     if (!p.wpk) prefetch_tmap(&tm_w);
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
       const int n0 = row0 + ch * 8;
       if (n0 + 8 <= p.N)
         *reinterpret_cast<uint4*>(rsd + t * NRO + ch * 8) =
-            *reinterpret_cast<const uint4*>(res + (int64_t)t * p.ldy + n0);
+            *reinterpret_cast<const uint4*>(res + (int64_t)(t0 + t) * p.ldy + n0);
     }
   }
   float acc[MT][NTM][4];
@@ -398,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = g8[i];
     }
-    T* yr = Y + (int64_t)t * p.ldy;
+    T* yr = Y + (int64_t)(t0 + t) * p.ldy;
     if (vec) {
       if (res) {
         float rf[8];
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
         *reinterpret_cast<uint4*>(p.ypk + ((size_t)(n0 >> 6) * BN + t) * 128 +
                                   ((((n0 >> 3) & 7) ^ (t & 7)) << 4)) = pk;
     } else {
-      const T* rr = res ? res + (int64_t)t * p.ldy : nullptr;
+      const T* rr = res ? res + (int64_t)(t0 + t) * p.ldy : nullptr;
       for (int i = 0; i < 8 && n0 + i < p.N; ++i) {
         float v = o[i];
         if (rr) v += to_f32(rr[n0 + i]);
@@ -429,18 +431,19 @@ __global__ void __launch_bounds__(kThreads, NTM <= 4 ? 2 : 1)
 
 template <typename T, int BN, int NTM, bool SW, bool NORM>
 int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
-              int nro) {
+              int nro, int tsplit) {
+  const size_t budget = BN == 16 ? kBudget16 : kBudget;
   using Plan = XsPlan<BN>;
   const int nr = SW ? 2 * nro : nro;
   const int nkb = (a.K + 63) / 64;
   // chunk: as many k-blocks as keep two stages within the budget, x part <= 32 KB
   int kc = 8;
   if (kc > nkb) kc = nkb;
-  while (kc > 1 && (BN * kc * 128 > 32768 || Plan::smem(nr, nro, kc, 2) > kBudget)) --kc;
-  if (Plan::smem(nr, nro, kc, nkb > kc ? 2 : 1) > kBudget) return -1;  // not applicable
+  while (kc > 1 && (BN * kc * 128 > 32768 || Plan::smem(nr, nro, kc, 2) > budget)) --kc;
+  if (Plan::smem(nr, nro, kc, nkb > kc ? 2 : 1) > budget) return -1;  // not applicable
   const int nch = (nkb + kc - 1) / kc;
   int stages = nch < kMaxStages ? nch : kMaxStages;
-  while (stages > 1 && Plan::smem(nr, nro, kc, stages) > kBudget) --stages;
+  while (stages > 1 && Plan::smem(nr, nro, kc, stages) > budget) --stages;
   a.nr = nr; a.kc = kc; a.nch = nch; a.stages = stages;
 #ifdef TPP_DEBUG_STAMPS
   a.dbg_id = g_xs_launch++;
@@ -495,20 +498,34 @@ int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, c
     }
     configured |= bit;
   }
-  return launch("linear_xs_kernel", kern, dim3((unsigned)ctas), dim3(kThreads),
+  return launch("linear_xs_kernel", kern, dim3((unsigned)ctas, (unsigned)tsplit), dim3(kThreads),
                 Plan::smem(nr, nro, kc, stages), st, 1u, tw, tx, a);
+}
+
+// Token split on unless TPP_XS_TSPLIT=0 (A/B measurements).
+bool tsplit_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TPP_XS_TSPLIT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 template <typename T, int NTM, bool NORM>
 int xs_dispatch_nt(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype,
                    cudaStream_t st, int nro) {
   const bool sw = a.act == TPP_ACT_SWIGLU;
-  if (a.M <= 16)
-    return sw ? launch_xs<T, 16, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro)
-              : launch_xs<T, 16, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro);
+  // 17..32 tokens: two CTAs per weight slice, 16 tokens each (twice the
+  // warps on the SMs, half the MMAs per CTA), unless the operands are packed
+  // (their layout is per 32-token tile) or the slice is wide.
+  const int tsplit = (a.M > 16 && NTM <= 4 && !a.wpk && !a.xpk && !a.ypk && tsplit_enabled())
+                         ? (a.M + 15) / 16 : 1;
+  if (a.M <= 16 || tsplit > 1)
+    return sw ? launch_xs<T, 16, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro, tsplit)
+              : launch_xs<T, 16, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro, tsplit);
   if (a.M <= 32)
-    return sw ? launch_xs<T, 32, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro)
-              : launch_xs<T, 32, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro);
+    return sw ? launch_xs<T, 32, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro, 1)
+              : launch_xs<T, 32, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro, 1);
   return -1;
 }
 
