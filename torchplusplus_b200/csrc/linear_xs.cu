@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
 template <typename T, int BN, int NTM, bool SW, bool NORM>
 int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
               int nro, int tsplit) {
-  const size_t budget = BN == 16 ? kBudget16 : kBudget;
+  const size_t budget = tsplit > 1 ? kBudget16 : kBudget;
   using Plan = XsPlan<BN>;
   const int nr = SW ? 2 * nro : nro;
   const int nkb = (a.K + 63) / 64;
