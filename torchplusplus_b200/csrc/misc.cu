@@ -30,7 +30,24 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, i
   };
   if (vec) {
     const int64_t nv = V / 8;
-    for (int64_t c = threadIdx.x; c < nv; c += blockDim.x) {
+    const int64_t step = blockDim.x;
+    int64_t c = threadIdx.x;
+    // four independent 16-byte loads in flight per thread (the logits were
+    // just written: each round trip is an L2 latency); order does not matter,
+    // ties are resolved by index
+    for (; c + 3 * step < nv; c += 4 * step) {
+      uint4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u[q] = ldg_nc_v4(row + (c + q * step) * 8);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float f[8];
+        unpack8<T>(u[q], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) take(f[j], (c + q * step) * 8 + j);
+      }
+    }
+    for (; c < nv; c += step) {
       float f[8];
       unpack8<T>(ldg_nc_v4(row + c * 8), f);
 #pragma unroll
