@@ -49,6 +49,13 @@ constexpr int kMaxNT = 8;                      // 8-row n-tiles per CTA (NR <= 6
 constexpr int kMaxStages = 4;
 constexpr size_t kBudget = 110 * 1024;  // two CTAs (of two kernels) per SM
 constexpr size_t kBudget16 = 72 * 1024; // 16-token tiles: three CTAs per SM
+constexpr size_t kBudget1 = 227 * 1024; // one CTA per SM
+
+bool tsplit_enabled();
+}  // namespace
+int xs_outputs_per_cta(int64_t N, int act);
+int xs_token_tile(int64_t M);
+namespace {
 
 struct XsArgs {
   const void* bias;
@@ -70,7 +77,6 @@ struct XsArgs {
   const uint8_t* wpk;
   const uint8_t* xpk;
   uint8_t* ypk;
-  int allow_wide;  // host-side choice only (see xs_dispatch)
 #ifdef TPP_DEBUG_STAMPS
   unsigned dbg_id;
 #endif
@@ -429,21 +435,21 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
 #endif
 }
 
+// Launch geometry chosen on the host (plan_xs).
+struct XsLaunch {
+  int nro;     // outputs per CTA
+  int bn;      // token tile (16 or 32)
+  int tsplit;  // token tiles (grid y)
+  int kc, nch, stages;
+};
+
 template <typename T, int BN, int NTM, bool SW, bool NORM>
 int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
-              int nro, int tsplit) {
-  const size_t budget = tsplit > 1 ? kBudget16 : kBudget;
+              const XsLaunch& L) {
   using Plan = XsPlan<BN>;
+  const int nro = L.nro, tsplit = L.tsplit, kc = L.kc, nch = L.nch, stages = L.stages;
   const int nr = SW ? 2 * nro : nro;
   const int nkb = (a.K + 63) / 64;
-  // chunk: as many k-blocks as keep two stages within the budget, x part <= 32 KB
-  int kc = 8;
-  if (kc > nkb) kc = nkb;
-  while (kc > 1 && (BN * kc * 128 > 32768 || Plan::smem(nr, nro, kc, 2) > budget)) --kc;
-  if (Plan::smem(nr, nro, kc, nkb > kc ? 2 : 1) > budget) return -1;  // not applicable
-  const int nch = (nkb + kc - 1) / kc;
-  int stages = nch < kMaxStages ? nch : kMaxStages;
-  while (stages > 1 && Plan::smem(nr, nro, kc, stages) > budget) --stages;
   a.nr = nr; a.kc = kc; a.nch = nch; a.stages = stages;
 #ifdef TPP_DEBUG_STAMPS
   a.dbg_id = g_xs_launch++;
@@ -492,7 +498,7 @@ int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, c
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kBudget) != cudaSuccess) {
+                             (int)kBudget1) != cudaSuccess) {
       set_error("linear_xs_kernel: cannot reserve shared memory");
       return TPP_ERR_LAUNCH;
     }
@@ -511,35 +517,103 @@ bool tsplit_enabled() {
   return on;
 }
 
+// Shared memory of a plan (XsPlan<BN>::smem with a runtime token tile).
+size_t xs_smem(int bn, int nr, int nro, int kc, int stages) {
+  const size_t ring = (size_t)stages * (nr + bn) * kc * 128;
+  const size_t red = (size_t)kCompute * bn * (nr + 4) * 4;
+  return 1024 + (ring > red ? ring : red) + 2048 + (((size_t)bn * nro * 2 + 15) & ~(size_t)15);
+}
+
+// Chunking for a given slice: one chunk (one request per operand, one memory
+// round trip) when the CTA's whole weight slice and x fit `limit`; else
+// chunks of up to 8 k-blocks (x part <= 32 KB) in a ring of >= 2 stages.
+bool xs_chunks(int bn, int nr, int nro, int nkb, size_t limit, size_t ring_limit, XsLaunch& L) {
+  if (nkb <= 256 && xs_smem(bn, nr, nro, nkb, 1) <= limit) {
+    L.kc = nkb; L.nch = 1; L.stages = 1;
+    return true;
+  }
+  int kc = nkb < 8 ? nkb : 8;
+  while (kc > 1 && (bn * kc * 128 > 32768 || xs_smem(bn, nr, nro, kc, 2) > ring_limit)) --kc;
+  if (xs_smem(bn, nr, nro, kc, nkb > kc ? 2 : 1) > ring_limit) return false;
+  L.kc = kc;
+  L.nch = (nkb + kc - 1) / kc;
+  L.stages = L.nch < kMaxStages ? L.nch : kMaxStages;
+  while (L.stages > 1 && xs_smem(bn, nr, nro, kc, L.stages) > ring_limit) --L.stages;
+  return true;
+}
+
+// Host plan for the unpacked path: among slice widths of 8..64 weight rows
+// (token-split into 16-token tiles where the register tile allows), keep
+// those whose grid fits one wave (two CTAs per SM within 110 KB of shared
+// memory, or one per SM within 227 KB) and take a single-chunk plan with
+// the fewest operand bytes per CTA; otherwise the multi-chunk fallback.
+bool plan_xs(int64_t M, int64_t N, int64_t K, int act, XsLaunch& out) {
+  const int sms = num_sms();
+  const int per_row = act == TPP_ACT_SWIGLU ? 2 : 1;
+  const int nkb = (int)(K / 64);
+  size_t best = ~(size_t)0;
+  for (int nro = 8; nro * per_row <= 8 * kMaxNT; nro += 8) {
+    const int nr = nro * per_row;
+    const int ntm = nr <= 16 ? 2 : (nr <= 32 ? 4 : 8);
+    const int tsplit = (M > 16 && ntm <= 4 && tsplit_enabled()) ? (int)((M + 15) / 16) : 1;
+    const int bn = (M <= 16 || tsplit > 1) ? 16 : 32;
+    const int64_t grid = (N + nro - 1) / nro * tsplit;
+    if (grid > 2 * (int64_t)sms) continue;
+    const size_t limit = grid <= sms ? kBudget1 : kBudget;
+    if (nkb > 256 || xs_smem(bn, nr, nro, nkb, 1) > limit) continue;
+    const size_t bytes = (size_t)(nr + bn) * nkb * 128;
+    if (bytes < best) {
+      best = bytes;
+      out.nro = nro; out.bn = bn; out.tsplit = tsplit;
+      out.kc = nkb; out.nch = 1; out.stages = 1;
+    }
+  }
+  if (best != ~(size_t)0) return true;
+  const int nro = xs_outputs_per_cta(N, act);
+  if (nro == 0) return false;
+  const int nr = nro * per_row;
+  const int ntm = nr <= 16 ? 2 : (nr <= 32 ? 4 : 8);
+  if (ntm > 4) return false;  // wide slices: the weight-streaming kernel does better
+  out.nro = nro;
+  out.tsplit = (M > 16 && tsplit_enabled()) ? (int)((M + 15) / 16) : 1;
+  out.bn = (M <= 16 || out.tsplit > 1) ? 16 : 32;
+  const int64_t grid = (N + nro - 1) / nro * out.tsplit;
+  return xs_chunks(out.bn, nr, nro, nkb, grid <= 2 * (int64_t)sms ? kBudget : 0,
+                   out.tsplit > 1 ? kBudget16 : kBudget, out);
+}
+
+// Packed operands: the slice width is fixed by the packed weight image
+// (xs_outputs_per_cta) and the token tile by the packed activation.
+bool plan_packed(int64_t M, int64_t N, int64_t K, int act, XsLaunch& out) {
+  const int nro = xs_outputs_per_cta(N, act);
+  if (nro == 0) return false;
+  const int nr = act == TPP_ACT_SWIGLU ? 2 * nro : nro;
+  out.nro = nro;
+  out.tsplit = 1;
+  out.bn = xs_token_tile(M);
+  const int64_t grid = (N + nro - 1) / nro;
+  return xs_chunks(out.bn, nr, nro, (int)(K / 64), grid <= 2 * (int64_t)num_sms() ? kBudget : 0,
+                   kBudget, out);
+}
+
 template <typename T, int NTM, bool NORM>
 int xs_dispatch_nt(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype,
-                   cudaStream_t st, int nro) {
+                   cudaStream_t st, const XsLaunch& L) {
   const bool sw = a.act == TPP_ACT_SWIGLU;
-  // 17..32 tokens: two CTAs per weight slice, 16 tokens each (twice the
-  // warps on the SMs, half the MMAs per CTA), unless the operands are packed
-  // (their layout is per 32-token tile) or the slice is wide.
-  const int tsplit = (a.M > 16 && NTM <= 4 && !a.wpk && !a.xpk && !a.ypk && tsplit_enabled())
-                         ? (a.M + 15) / 16 : 1;
-  if (a.M <= 16 || tsplit > 1)
-    return sw ? launch_xs<T, 16, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro, tsplit)
-              : launch_xs<T, 16, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro, tsplit);
-  if (a.M <= 32)
-    return sw ? launch_xs<T, 32, NTM, true, NORM>(x, ldx, w, a, dtype, st, nro, 1)
-              : launch_xs<T, 32, NTM, false, NORM>(x, ldx, w, a, dtype, st, nro, 1);
-  return -1;
+  if (L.bn == 16)
+    return sw ? launch_xs<T, 16, NTM, true, NORM>(x, ldx, w, a, dtype, st, L)
+              : launch_xs<T, 16, NTM, false, NORM>(x, ldx, w, a, dtype, st, L);
+  return sw ? launch_xs<T, 32, NTM, true, NORM>(x, ldx, w, a, dtype, st, L)
+            : launch_xs<T, 32, NTM, false, NORM>(x, ldx, w, a, dtype, st, L);
 }
 
 template <typename T, bool NORM>
 int xs_dispatch(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
-                int nro) {
-  const int nt = (a.act == TPP_ACT_SWIGLU ? 2 * nro : nro) / 8;
-  if (nt <= 2) return xs_dispatch_nt<T, 2, NORM>(x, ldx, w, a, dtype, st, nro);
-  if (nt <= 4) return xs_dispatch_nt<T, 4, NORM>(x, ldx, w, a, dtype, st, nro);
-  // Wider slices only fit one CTA per SM, which also keeps the next kernel's
-  // CTAs from starting early; the packed entry point still takes them, the
-  // plain decode dispatch prefers the weight-streaming kernel (a.allow_wide).
-  if (!a.allow_wide) return -1;
-  return xs_dispatch_nt<T, 8, NORM>(x, ldx, w, a, dtype, st, nro);
+                const XsLaunch& L) {
+  const int nt = (a.act == TPP_ACT_SWIGLU ? 2 * L.nro : L.nro) / 8;
+  if (nt <= 2) return xs_dispatch_nt<T, 2, NORM>(x, ldx, w, a, dtype, st, L);
+  if (nt <= 4) return xs_dispatch_nt<T, 4, NORM>(x, ldx, w, a, dtype, st, L);
+  return xs_dispatch_nt<T, 8, NORM>(x, ldx, w, a, dtype, st, L);
 }
 
 }  // namespace
@@ -583,8 +657,9 @@ int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
   // The 3-D views address k-block kb of a row at +128 * kb bytes: rows must
   // be whole k-blocks, or the last one would run into the next row.
   if (K % 64 != 0 || M > 32) return -1;
-  const int nro = xs_outputs_per_cta(N, act);
-  if (nro == 0) return -1;
+  XsLaunch L;
+  const bool packed = wpk || xpk || ypk;
+  if (!(packed ? plan_packed(M, N, K, act, L) : plan_xs(M, N, K, act, L))) return -1;
   XsArgs a;
   a.bias = bias; a.residual = residual; a.y = y; a.ldy = ldy;
   a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act;
@@ -595,10 +670,9 @@ int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
   a.wpk = static_cast<const uint8_t*>(wpk);
   a.xpk = static_cast<const uint8_t*>(xpk);
   a.ypk = static_cast<uint8_t*>(ypk);
-  a.allow_wide = wpk != nullptr;
   return TPP_DISPATCH_HALF(dtype, T, [&] {
-    return norm_eps >= 0.f ? xs_dispatch<T, true>(x, ldx, w, a, dtype, st, nro)
-                           : xs_dispatch<T, false>(x, ldx, w, a, dtype, st, nro);
+    return norm_eps >= 0.f ? xs_dispatch<T, true>(x, ldx, w, a, dtype, st, L)
+                           : xs_dispatch<T, false>(x, ldx, w, a, dtype, st, L);
   });
 }
 
