@@ -43,9 +43,9 @@ PROMPT, GEN = 512, 256
 
 
 # DRAM bytes (read + write) per decode-linear launch, measured by ncu on this
-# bench's own command (profiles/decode_linears_dram_qwen3_b32.md): 10.797 MB
+# bench's own command (profiles/decode_linears_dram_qwen3_b32.md): 10.787 MB
 # against 10.93 MB algorithmic -- the weights are read once.
-LINEAR_DRAM_BYTES_PER_LAUNCH = 10.797e6
+LINEAR_DRAM_BYTES_PER_LAUNCH = 10.787e6
 
 
 def peaks():
@@ -389,8 +389,8 @@ def run_ours(args, rank, world, local):
     rl = linear_roofline(eng)
     peak, peak_kind = peaks()
     achieved = rl["bytes_per_launch"] / rl["avg_launch_s"] / 1e9
-    roofline = {"kernel": "decode linears: linear_xs_kernel (qkv, o, down) and "
-                          "linear_skinny_kernel (gate/up, LM head), 113 launches per step",
+    roofline = {"kernel": "decode linears: linear_xs_kernel (qkv, o, gate/up, down) and "
+                          "linear_skinny_kernel (LM head), 113 launches per step",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind}",
                 "traffic": LINEAR_DRAM_BYTES_PER_LAUNCH,
