@@ -40,8 +40,11 @@
 namespace tpp {
 namespace {
 
-constexpr int kCompute = 8;                    // compute warps
-constexpr int kThreads = (kCompute + 1) * 32;  // + the producer warp
+// Compute warps per CTA (plus one producer warp).  Kept a function of the
+// register tile: 12 or 16 warps for the wide slices measured no faster (16
+// spill at the 544-thread register cap).
+__host__ __device__ constexpr int xs_warps(int) { return 8; }
+__host__ __device__ constexpr int xs_threads(int ntm) { return (xs_warps(ntm) + 1) * 32; }
 constexpr int kMaxNT = 8;                      // 8-row n-tiles per CTA (NR <= 64)
 // Register tiles are sized for NTM n-tiles (2, 4 or 8).  Up to 4 the kernel
 // fits two CTAs per SM, so the next kernel's CTA can be resident (and
@@ -93,17 +96,17 @@ unsigned g_xs_launch = 0;
 #define XS_TS(i) do {} while (0)
 #endif
 
-template <int BN>
+template <int BN, int KW>
 struct XsPlan {
   __host__ __device__ static uint32_t stage(int nr, int kc) { return (uint32_t)(nr + BN) * kc * 128; }
-  __host__ __device__ static uint32_t red(int nr) { return (uint32_t)kCompute * BN * (nr + 4) * 4; }
+  __host__ __device__ static uint32_t red(int nr) { return (uint32_t)KW * BN * (nr + 4) * 4; }
   static uint32_t rsd(int nro) { return ((uint32_t)BN * nro * 2 + 15) & ~15u; }
   __host__ __device__ static size_t ring(int nr, int kc, int stages) {
     const size_t r = (size_t)stages * stage(nr, kc);
     return r > red(nr) ? r : red(nr);
   }
   static size_t smem(int nr, int nro, int kc, int stages) {
-    return 1024 + ring(nr, kc, stages) + 2048 + rsd(nro);
+    return 1024 + ring(nr, kc, stages) + 4096 + rsd(nro);
   }
 };
 
@@ -116,10 +119,11 @@ __device__ __forceinline__ float sq2(uint32_t v) {
 }
 
 template <typename T, int BN, int NTM, bool SWIGLU, bool NORM>
-__global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
+__global__ void __launch_bounds__(xs_threads(NTM), NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
     linear_xs_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_x, XsArgs p) {
   constexpr int MT = BN / 16;  // m-tiles (16 tokens)
+  constexpr int KW = xs_warps(NTM);  // compute warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
@@ -130,12 +134,12 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
   const uint32_t wbytes = (uint32_t)NR * KC * 128;
   const uint32_t xbytes = (uint32_t)BN * KC * 128;
   const uint32_t sbytes = wbytes + xbytes;
-  uint8_t* misc = smem + XsPlan<BN>::ring(NR, KC, S);
+  uint8_t* misc = smem + XsPlan<BN, KW>::ring(NR, KC, S);
   uint64_t* full = reinterpret_cast<uint64_t*>(misc);
   uint64_t* empty = full + kMaxStages;
-  float* ssw = reinterpret_cast<float*>(misc + 128);  // [kCompute][BN] sums of squares (1 KB)
-  T* rsd = reinterpret_cast<T*>(misc + 2048);         // [BN][NRO] residual slice
-  float* red = reinterpret_cast<float*>(smem);        // [kCompute][BN][RST], after the ring
+  float* ssw = reinterpret_cast<float*>(misc + 128);  // [KW][BN] sums of squares (<= 2 KB)
+  T* rsd = reinterpret_cast<T*>(misc + 4096);         // [BN][NRO] residual slice
+  float* red = reinterpret_cast<float*>(smem);        // [KW][BN][RST], after the ring
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * NRO;  // first output (and weight row) of this CTA
@@ -150,13 +154,13 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
     XS_TS(0);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCompute);
+      mbar_init(&empty[s], KW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == kCompute) {
+  if (warp == KW) {
     // ---------------- TMA / bulk producer ----------------
     if (lane != 0) return;
     bool ok = true;
@@ -215,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
   if (p.residual && p.vec_ok) {
     const T* res = static_cast<const T*>(p.residual);
     const int chunks = NRO / 8;
-    for (int e = tid; e < mt * chunks; e += kCompute * 32) {
+    for (int e = tid; e < mt * chunks; e += KW * 32) {
       const int t = e / chunks, ch = e % chunks;
       const int n0 = row0 + ch * 8;
       if (n0 + 8 <= p.N)
@@ -232,9 +236,9 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
       for (int q = 0; q < 4; ++q) acc[mi][ni][q] = 0.f;
   float ssl[MT][2] = {};
   bool ok = true;
-  // Warp w takes k16 step (w % 4) of every (kCompute / 4)-th k-block of each
+  // Warp w takes k16 step (w % 4) of every (KW / 4)-th k-block of each
   // chunk.
-  constexpr int kJStep = kCompute / 4;  // k-block stride of one warp
+  constexpr int kJStep = KW / 4;  // k-block stride of one warp
   const int kk = warp & 3, jpar = warp >> 2;
   // Per-thread ldmatrix offsets inside a k-block tile (constant: this warp
   // always reads the same k16 step); 128-byte swizzle: 16-byte chunk q of
@@ -303,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
 
   // ---------------- cross-warp reduction ----------------
   if (threadIdx.x == 0) XS_TS(8);
-  asm volatile("bar.sync 1, %0;" ::"n"(kCompute * 32) : "memory");  // ring no longer read
+  asm volatile("bar.sync 1, %0;" ::"n"(KW * 32) : "memory");  // ring no longer read
   if (threadIdx.x == 0) XS_TS(9);
   {
     const int g = lane >> 2, cq = lane & 3;
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
       }
     }
   }
-  asm volatile("bar.sync 1, %0;" ::"n"(kCompute * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(KW * 32) : "memory");
   if (threadIdx.x == 0) XS_TS(10);
 
   // ---------------- epilogue ----------------
@@ -340,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
   T* Y = static_cast<T*>(p.y);
   const int groups = NRO / 8;
   const float inv_k = 1.0f / (float)p.K;
-  for (int e = tid; e < mt * groups; e += kCompute * 32) {
+  for (int e = tid; e < mt * groups; e += KW * 32) {
     const int t = e / groups, c0 = (e % groups) * 8;
     const int n0 = row0 + c0;
     if (n0 >= p.N) continue;
@@ -348,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
     if (NORM) {
       float ss = 0.f;
 #pragma unroll
-      for (int w = 0; w < kCompute; ++w) ss += ssw[w * BN + t];
+      for (int w = 0; w < KW; ++w) ss += ssw[w * BN + t];
       rs = rsqrtf(ss * inv_k + p.eps);
     }
     if (threadIdx.x == 0) XS_TS(6);
@@ -356,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, NTM > 4 ? 1 : (BN == 16 ? 3 : 2))
 #pragma unroll
     for (int i = 0; i < 8; ++i) { g8[i] = 0.f; u8[i] = 0.f; }
 #pragma unroll
-    for (int w = 0; w < kCompute; ++w) {
+    for (int w = 0; w < KW; ++w) {
       const float* rr = red + (w * BN + t) * RST + c0;
       const float4 p0 = *reinterpret_cast<const float4*>(rr);
       const float4 p1 = *reinterpret_cast<const float4*>(rr + 4);
@@ -446,7 +450,7 @@ struct XsLaunch {
 template <typename T, int BN, int NTM, bool SW, bool NORM>
 int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, cudaStream_t st,
               const XsLaunch& L) {
-  using Plan = XsPlan<BN>;
+  using Plan = XsPlan<BN, xs_warps(NTM)>;
   const int nro = L.nro, tsplit = L.tsplit, kc = L.kc, nch = L.nch, stages = L.stages;
   const int nr = SW ? 2 * nro : nro;
   const int nkb = (a.K + 63) / 64;
@@ -504,7 +508,7 @@ int launch_xs(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype, c
     }
     configured |= bit;
   }
-  return launch("linear_xs_kernel", kern, dim3((unsigned)ctas, (unsigned)tsplit), dim3(kThreads),
+  return launch("linear_xs_kernel", kern, dim3((unsigned)ctas, (unsigned)tsplit), dim3(xs_threads(NTM)),
                 Plan::smem(nr, nro, kc, stages), st, 1u, tw, tx, a);
 }
 
@@ -519,9 +523,10 @@ bool tsplit_enabled() {
 
 // Shared memory of a plan (XsPlan<BN>::smem with a runtime token tile).
 size_t xs_smem(int bn, int nr, int nro, int kc, int stages) {
+  const int ntm = nr <= 16 ? 2 : (nr <= 32 ? 4 : 8);
   const size_t ring = (size_t)stages * (nr + bn) * kc * 128;
-  const size_t red = (size_t)kCompute * bn * (nr + 4) * 4;
-  return 1024 + (ring > red ? ring : red) + 2048 + (((size_t)bn * nro * 2 + 15) & ~(size_t)15);
+  const size_t red = (size_t)xs_warps(ntm) * bn * (nr + 4) * 4;
+  return 1024 + (ring > red ? ring : red) + 4096 + (((size_t)bn * nro * 2 + 15) & ~(size_t)15);
 }
 
 // Chunking for a given slice: one chunk (one request per operand, one memory
