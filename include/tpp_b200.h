@@ -163,6 +163,11 @@ int tpp_linear_packed(const void* x_packed, const void* w_packed, const void* bi
                       const void* residual, void* y, int64_t ldy, void* y_packed, int64_t M,
                       int64_t N, int64_t K, float eps, int act, int dtype, void* stream);
 
+/* Bulk-prefetch [ptr, ptr + bytes) into L2 (16-byte aligned, bytes % 16 ==
+ * 0); no data reaches the SMs.  Meant for a parallel branch of a decode
+ * graph that warms the next layers' weights.  No reference counterpart. */
+int tpp_l2_prefetch(const void* ptr, int64_t bytes, void* stream);
+
 /* y[N] = W[N,K] . x[K]   (fp32 accumulation; y in dtype)
  * Replaces launchHgemv / launchHgemvCute (hgemv_kernels.cuh:69-85, 240-262),
  * which accumulated in fp16. */

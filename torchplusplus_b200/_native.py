@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_rmsnorm_linear": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _i32,
                                   _i32, _p]),
     "tpp_hgemv": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
+    "tpp_l2_prefetch": (_i32, [_p, _i64, _p]),
     "tpp_packed_weight_bytes": (_i64, [_i64, _i64, _i32]),
     "tpp_packed_activation_bytes": (_i64, [_i64, _i64]),
     "tpp_pack_weight": (_i32, [_p, _i64, _i64, _i32, _i32, _p, _p]),

@@ -164,3 +164,37 @@ extern "C" int tpp_embedding(const int64_t* ids, int64_t T_, const void* table, 
         ids, T_, (const T*)table, V, D, (T*)out, vec);
   });
 }
+
+// ---------------------------------------------------------------------------
+// L2 warm-up: bulk prefetch of [ptr, ptr + bytes) into L2 (no data is moved
+// to the SMs).  A decode engine launches it on a parallel graph branch so the
+// next layers' weights are L2 hits when their kernels load them.
+// ---------------------------------------------------------------------------
+namespace tpp {
+namespace {
+__global__ void l2_prefetch_kernel(const uint8_t* __restrict__ p, int64_t bytes) {
+  constexpr int64_t kPiece = 64 * 1024;
+  const int64_t n = (bytes + kPiece - 1) / kPiece;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t off = i * kPiece;
+    const int64_t len = bytes - off < kPiece ? bytes - off : kPiece;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"((uint32_t)len)
+                 : "memory");
+  }
+}
+}  // namespace
+}  // namespace tpp
+
+extern "C" int tpp_l2_prefetch(const void* ptr, int64_t bytes, void* stream) {
+  if (bytes <= 0) return TPP_OK;
+  TPP_REQUIRE(ptr, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(aligned16(ptr) && bytes % 16 == 0, TPP_ERR_ALIGN,
+              "prefetch range must be 16-byte aligned and a multiple of 16 bytes");
+  const int64_t pieces = (bytes + 65535) / 65536;
+  const int threads = 32;
+  const int blocks = (int)((pieces + threads - 1) / threads < 64 ? (pieces + threads - 1) / threads : 64);
+  l2_prefetch_kernel<<<blocks, threads, 0, as_stream(stream)>>>(static_cast<const uint8_t*>(ptr),
+                                                                bytes);
+  return check_launch("l2_prefetch_kernel");
+}

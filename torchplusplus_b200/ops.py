@@ -280,6 +280,13 @@ def linear_packed(x_packed: torch.Tensor, M: int, w: PackedWeight,
     return out
 
 
+def l2_prefetch(t: torch.Tensor) -> None:
+    """Bulk-prefetch a (contiguous) tensor's bytes into L2 on the current stream."""
+    _cuda(t)
+    n = t.numel() * t.element_size()
+    N.call("tpp_l2_prefetch", t.data_ptr(), n - n % 16, N.stream_of(t))
+
+
 def hgemv(weight: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """y[N] = weight[N,K] @ x[K] with fp32 accumulation."""
     _cuda(weight, x)
