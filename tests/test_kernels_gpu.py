@@ -139,10 +139,30 @@ def _linear_case(M, N, K, act, dtype, bias=False, residual=False, seed=8):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("M", [1, 7, 32, 64])
+@pytest.mark.parametrize("M", [1, 7, 17, 20, 31, 32, 64])
 @pytest.mark.parametrize("act", ["none", "silu", "gelu", "relu", "swiglu"])
 def test_linear_decode_shapes(dtype, M, act):
+    # 17..32 tokens exercise the two-tile (16 + up to 16 tokens) decode grids
     _linear_case(M, 3072, 1024, act, dtype)
+
+
+@pytest.mark.parametrize("MNK", [(32, 1024, 3072), (20, 1024, 2048), (32, 4096, 1024),
+                                 (9, 6144, 1024), (32, 640, 4096)])
+def test_linear_decode_planned_shapes_bias_residual(MNK):
+    """Slice widths, token split and single- vs multi-chunk plans of the
+    x-stationary decode linear, with bias and residual."""
+    M, N, K = MNK
+    _linear_case(M, N, K, "none", torch.bfloat16, bias=True, residual=True, seed=21)
+
+
+def test_l2_prefetch_leaves_data_unchanged():
+    g = gen(22)
+    w = rnd(4096, 1024, g=g, dtype=torch.bfloat16).to(DEV)
+    before = w.clone()
+    ops.l2_prefetch(w)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(w, before)
 
 
 @pytest.mark.parametrize("MNK", [(1, 1024, 3072), (5, 1000, 200), (32, 2048, 2048),
