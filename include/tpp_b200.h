@@ -232,6 +232,38 @@ int tpp_attention_decode_qkv(const void* qkv, int64_t ld_qkv, const void* qn_w,
                              int64_t D, int64_t window_left, float scale, void* workspace,
                              int64_t workspace_bytes, int dtype, void* stream);
 
+/* ---- paged KV cache --------------------------------------------------------
+ * K and V live in block pools [num_blocks][Hkv][64][D] (64 keys a block);
+ * sequence b's key k sits in block block_table[b * table_stride + k / 64],
+ * row k % 64.  The decode kernels read one 64-key tile per block with one
+ * TMA request.  Blocks must exist for every position < seqlens[b].  No
+ * reference counterpart (the reference lists a paged cache as a TODO,
+ * todo.md:8); semantics as the contiguous entry points. */
+int tpp_attention_decode_paged(const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool,
+                               const void* v_pool, int64_t num_blocks,
+                               const int32_t* block_table, int64_t table_stride,
+                               const int32_t* seqlens, int64_t max_seqlen, void* o,
+                               int64_t o_sb, int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv,
+                               int64_t D, int64_t window_left, float scale, void* workspace,
+                               int64_t workspace_bytes, int dtype, void* stream);
+int tpp_attention_decode_qkv_paged(const void* qkv, int64_t ld_qkv, const void* qn_w,
+                                   const void* kn_w, float eps, const void* cos, const void* sin,
+                                   int64_t cs_stride, int cs_dtype, const int32_t* positions,
+                                   void* k_pool, void* v_pool, int64_t num_blocks,
+                                   const int32_t* block_table, int64_t table_stride,
+                                   const int32_t* seqlens, int64_t max_seqlen, void* o,
+                                   int64_t o_sb, int64_t o_sh, int64_t B, int64_t Hq,
+                                   int64_t Hkv, int64_t D, int64_t window_left, float scale,
+                                   void* workspace, int64_t workspace_bytes, int dtype,
+                                   void* stream);
+/* Prompt K/V [B, Hkv, S, D] (element strides) into the pools at positions
+ * (positions[b] if given, else start_pos) + s. */
+int tpp_kv_append_paged(const void* k, int64_t k_sb, int64_t k_sh, int64_t k_ss, const void* v,
+                        int64_t v_sb, int64_t v_sh, int64_t v_ss, void* k_pool, void* v_pool,
+                        int64_t num_blocks, const int32_t* block_table, int64_t table_stride,
+                        const int32_t* positions, int64_t start_pos, int64_t B, int64_t Hkv,
+                        int64_t S, int64_t D, int dtype, void* stream);
+
 /* Allocation-free decode attention: the same computation and arguments as
  * tpp_attention_decode, minus the workspace.  For callers that cannot
  * allocate device memory when they decode (allocator / memory-pool

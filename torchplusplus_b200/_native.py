@@ -67,6 +67,14 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_attention_decode_qkv": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _i32, _p, _p, _p,
                                         _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64,
                                         _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
+    "tpp_attention_decode_paged": (_i32, [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p,
+                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p,
+                                          _i64, _i32, _p]),
+    "tpp_attention_decode_qkv_paged": (_i32, [_p, _i64, _p, _p, _f32, _p, _p, _i64, _i32, _p, _p,
+                                              _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64,
+                                              _i64, _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
+    "tpp_kv_append_paged": (_i32, [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _i64, _p,
+                                   _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p]),
     "tpp_attention_decode": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i64,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _i32, _p]),
     "tpp_attention_decode_noalloc": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i64,

@@ -289,16 +289,28 @@ struct FusedQkv {
   const int32_t* positions;
 };
 
+// Paged caches (see DecMmaArgs): block pools [num_blocks][Hkv][64][D].
+struct PagedKv {
+  const int32_t* table; int64_t tbl_stride; int64_t num_blocks;
+};
+
 int attn_decode_run(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cache,
                     const void* v_cache, int64_t c_sb, int64_t c_sh, int64_t c_ss,
                     const int32_t* seqlens, int64_t max_seqlen, void* o, int64_t o_sb,
                     int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                     int64_t window_left, float scale, void* ws, int64_t ws_bytes, int dtype,
-                    cudaStream_t st, const FusedQkv* fz = nullptr) {
+                    cudaStream_t st, const FusedQkv* fz = nullptr, const PagedKv* pg = nullptr) {
   if (B == 0) return TPP_OK;
   TPP_REQUIRE((q || fz) && k_cache && v_cache && o, TPP_ERR_SHAPE, "null pointer");
   TPP_REQUIRE(!fz || D == 64 || D == 128, TPP_ERR_UNSUPPORTED,
               "the fused q/k norm + RoPE decode path needs head dim 64 or 128");
+  TPP_REQUIRE(!pg || D == 64 || D == 128, TPP_ERR_UNSUPPORTED,
+              "paged decode attention needs head dim 64 or 128");
+  if (pg) {  // pool layout is fixed: strides implied
+    TPP_REQUIRE(pg->table && pg->num_blocks > 0 && pg->tbl_stride >= (max_seqlen + 63) / 64,
+                TPP_ERR_SHAPE, "block table must cover max_seqlen (64-key blocks)");
+    c_ss = D; c_sh = 64 * D; c_sb = Hkv * 64 * D;
+  }
   TPP_REQUIRE(B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, TPP_ERR_SHAPE,
               "Hq must be a positive multiple of Hkv");
   TPP_REQUIRE(D == 64 || D == 128 || D == 256, TPP_ERR_UNSUPPORTED, "head dim must be 64, 128 or 256");
@@ -321,6 +333,9 @@ int attn_decode_run(const void* q, int64_t q_sb, int64_t q_sh, const void* k_cac
       m.positions = fz->positions;
       m.kc = const_cast<void*>(k_cache); m.vc = const_cast<void*>(v_cache);
       m.c_sb = c_sb; m.c_sh = c_sh; m.c_ss = c_ss;
+    }
+    if (pg) {
+      m.table = pg->table; m.tbl_stride = pg->tbl_stride; m.num_blocks = pg->num_blocks;
     }
     m.o = o; m.o_sb = o_sb; m.o_sh = o_sh;
     m.seqlens = seqlens; m.max_seqlen = max_seqlen;
@@ -424,6 +439,40 @@ extern "C" int tpp_attention_decode_qkv(
   return attn_decode_run(nullptr, 0, 0, k_cache, v_cache, c_sb, c_sh, c_ss, seqlens, max_seqlen,
                          o, o_sb, o_sh, B, Hq, Hkv, D, window_left, scale, workspace,
                          workspace_bytes, dtype, as_stream(stream), &fz);
+}
+
+extern "C" int tpp_attention_decode_paged(
+    const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool, const void* v_pool,
+    int64_t num_blocks, const int32_t* block_table, int64_t table_stride,
+    const int32_t* seqlens, int64_t max_seqlen, void* o, int64_t o_sb, int64_t o_sh, int64_t B,
+    int64_t Hq, int64_t Hkv, int64_t D, int64_t window_left, float scale, void* workspace,
+    int64_t workspace_bytes, int dtype, void* stream) {
+  if (B == 0) return TPP_OK;
+  TPP_REQUIRE(seqlens, TPP_ERR_SHAPE, "paged decode needs per-sequence lengths");
+  PagedKv pg{block_table, table_stride, num_blocks};
+  return attn_decode_run(q, q_sb, q_sh, k_pool, v_pool, 0, 0, 0, seqlens, max_seqlen, o, o_sb,
+                         o_sh, B, Hq, Hkv, D, window_left, scale, workspace, workspace_bytes,
+                         dtype, as_stream(stream), nullptr, &pg);
+}
+
+extern "C" int tpp_attention_decode_qkv_paged(
+    const void* qkv, int64_t ld_qkv, const void* qn_w, const void* kn_w, float eps,
+    const void* cos, const void* sin, int64_t cs_stride, int cs_dtype,
+    const int32_t* positions, void* k_pool, void* v_pool, int64_t num_blocks,
+    const int32_t* block_table, int64_t table_stride, const int32_t* seqlens,
+    int64_t max_seqlen, void* o, int64_t o_sb, int64_t o_sh, int64_t B, int64_t Hq, int64_t Hkv,
+    int64_t D, int64_t window_left, float scale, void* workspace, int64_t workspace_bytes,
+    int dtype, void* stream) {
+  if (B == 0) return TPP_OK;
+  TPP_REQUIRE(qkv && cos && sin && positions && seqlens, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(cs_dtype == TPP_F16, TPP_ERR_DTYPE, "RoPE tables must be fp16 (compute_rope_params)");
+  TPP_REQUIRE(ld_qkv >= (Hq + 2 * Hkv) * D, TPP_ERR_SHAPE, "qkv row shorter than (Hq+2Hkv)*D");
+  TPP_REQUIRE(cs_stride >= D, TPP_ERR_SHAPE, "RoPE table row shorter than D");
+  FusedQkv fz{qkv, ld_qkv, qn_w, kn_w, eps, cos, sin, cs_stride, positions};
+  PagedKv pg{block_table, table_stride, num_blocks};
+  return attn_decode_run(nullptr, 0, 0, k_pool, v_pool, 0, 0, 0, seqlens, max_seqlen, o, o_sb,
+                         o_sh, B, Hq, Hkv, D, window_left, scale, workspace, workspace_bytes,
+                         dtype, as_stream(stream), &fz, &pg);
 }
 
 // ---------------------------------------------------------------------------

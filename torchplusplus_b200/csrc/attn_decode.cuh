@@ -28,6 +28,10 @@ struct DecMmaArgs {
   const void* cosp; const void* sinp; int64_t cs_stride;  // fp16 tables [ctx, D]
   const int32_t* positions;
   void* kc; void* vc; int64_t c_sb, c_sh, c_ss;           // cache (element strides)
+  // Paged mode (table != nullptr): the caches are block pools
+  // [num_blocks][Hkv][64][D]; key k of sequence b lives in block
+  // table[b * tbl_stride + k / 64], row k % 64.
+  const int32_t* table; int64_t tbl_stride; int64_t num_blocks;
 #ifdef TPP_DEBUG_STAMPS
   unsigned dbg_id;
 #endif

@@ -126,10 +126,14 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   const int64_t L = p.seqlens ? (int64_t)p.seqlens[b] : p.max_seqlen;
   int64_t lo = 0;
   if (p.window_left >= 0) lo = max((int64_t)0, L - 1 - p.window_left);
-  const int64_t n = L > lo ? L - lo : 0;
+  // Paged caches: a tile is one 64-key block, so the split ranges start on a
+  // block boundary and keys below lo are masked.
+  const bool paged = p.table != nullptr;
+  const int64_t lo_t = paged ? lo / KT * KT : lo;
+  const int64_t n = L > lo_t ? L - lo_t : 0;
   int64_t per = (n + p.splits - 1) / p.splits;
   per = (per + KT - 1) / KT * KT;
-  const int64_t k0 = lo + (int64_t)split * per;
+  const int64_t k0 = lo_t + (int64_t)split * per;
   const int64_t k1c = min(L, k0 + per);
   // Fused mode: the CTA whose key range holds the new token's position takes
   // that key from registers (normalised, rotated) rather than from the cache
@@ -143,12 +147,19 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     const int s = i % kStages;
     uint8_t* kd = ring + s * 2 * SM::kTile;
     uint8_t* vd = kd + SM::kTile;
-    const int key = (int)(k0 + (int64_t)i * KT);
+    const int64_t key = k0 + (int64_t)i * KT;
     mbar_arrive_expect_tx(&full[s], 2 * SM::kTile);
     // one request per operand: the D/64 column boxes of the tile come from a
-    // 5-D view {64, key, D/64, kv head, batch}
-    tma_load_5d(kd, &tm_k, &full[s], 0, key, 0, kvh, b);
-    tma_load_5d(vd, &tm_v, &full[s], 0, key, 0, kvh, b);
+    // 5-D view {64, key, D/64, kv head, batch} (paged: {64, row in block,
+    // D/64, kv head, block})
+    if (paged) {
+      const int blk = p.table[b * p.tbl_stride + key / KT];
+      tma_load_5d(kd, &tm_k, &full[s], 0, 0, 0, kvh, blk);
+      tma_load_5d(vd, &tm_v, &full[s], 0, 0, 0, kvh, blk);
+    } else {
+      tma_load_5d(kd, &tm_k, &full[s], 0, (int)key, 0, kvh, b);
+      tma_load_5d(vd, &tm_v, &full[s], 0, (int)key, 0, kvh, b);
+    }
   };
   if (tid == 0) {
     for (int i = 0; i < ntiles && i < kStages; ++i) issue(i);
@@ -281,7 +292,11 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
           vnew[lane * EPL + j] = to_f32(rv[j]);
         }
         if (pass == 0) {
-          const int64_t off = b * p.c_sb + kvh * p.c_sh + pos * p.c_ss + lane * EPL;
+          const int64_t off =
+              (paged ? ((int64_t)p.table[b * p.tbl_stride + pos / KT] * p.Hkv + kvh) * (KT * D) +
+                           (pos % KT) * D
+                     : b * p.c_sb + kvh * p.c_sh + pos * p.c_ss) +
+              lane * EPL;
           *reinterpret_cast<VT*>(static_cast<T*>(p.kc) + off) = pk;
           *reinterpret_cast<VT*>(static_cast<T*>(p.vc) + off) = pv;
         }
@@ -358,7 +373,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int64_t key = kbase + j * 8 + 2 * c + (e & 1);
-        sc[j][e] = key < k1 ? sc[j][e] * p.scale_log2 : -INFINITY;
+        sc[j][e] = (key < k1 && key >= lo) ? sc[j][e] * p.scale_log2 : -INFINITY;
       }
     float corr[2];
 #pragma unroll
@@ -605,9 +620,14 @@ int decode_mma_launch(DecMmaArgs& a, const void* k_cache, const void* v_cache, i
   CUtensorMap tk, tv;
   const uint64_t smax = (uint64_t)(a.max_seqlen > 0 ? a.max_seqlen : 1);
   // {64 columns, key, column box (D/64), kv head, batch}: the tile's column
-  // boxes land one after another ([box][key][128 B]), as the kernel reads them
-  const uint64_t dims[5] = {64, smax, (uint64_t)(D / 64), (uint64_t)a.Hkv, (uint64_t)B};
-  const uint64_t strides[4] = {(uint64_t)c_ss * 2, 128, (uint64_t)c_sh * 2, (uint64_t)c_sb * 2};
+  // boxes land one after another ([box][key][128 B]), as the kernel reads
+  // them.  Paged pools [block][Hkv][64][D]: {64, row, D/64, kv head, block}.
+  const bool paged = a.table != nullptr;
+  const uint64_t dims[5] = {64, paged ? (uint64_t)KT : smax, (uint64_t)(D / 64), (uint64_t)a.Hkv,
+                            paged ? (uint64_t)a.num_blocks : (uint64_t)B};
+  const uint64_t strides[4] = {
+      (uint64_t)D * 2, 128, paged ? (uint64_t)KT * D * 2 : (uint64_t)c_sh * 2,
+      paged ? (uint64_t)a.Hkv * KT * D * 2 : (uint64_t)c_sb * 2};
   const uint32_t box[5] = {64, KT, (uint32_t)(D / 64), 1, 1};
   int rc = make_tmap(&tk, k_cache, dtype, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TPP_OK) return rc;

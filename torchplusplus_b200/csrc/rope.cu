@@ -321,6 +321,62 @@ static int qnrc_launch(const void* qkv, int64_t ld, const void* qn, const void* 
   }
 }
 
+namespace tpp {
+namespace {
+// K/V rows [B, Hkv, S, D] (strided) -> paged pools [num_blocks][Hkv][64][D]
+// at positions (positions[b] or start_pos) + s, block table lookup per row.
+template <typename T>
+__global__ void __launch_bounds__(256) kv_append_paged_kernel(
+    const T* __restrict__ k, int64_t k_sb, int64_t k_sh, int64_t k_ss, const T* __restrict__ v,
+    int64_t v_sb, int64_t v_sh, int64_t v_ss, T* __restrict__ kp, T* __restrict__ vp,
+    const int32_t* __restrict__ table, int64_t tbl_stride, int64_t Hkv, int64_t S, int D,
+    int64_t start_pos, const int32_t* __restrict__ positions, int64_t total) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int per_row = D / 8;
+  const int c = (int)(idx % per_row);
+  const int64_t row = idx / per_row;
+  const int64_t s = row % S;
+  const int64_t bh = row / S;
+  const int64_t h = bh % Hkv;
+  const int64_t b = bh / Hkv;
+  const int64_t pos = (positions ? (int64_t)positions[b] : start_pos) + s;
+  const int64_t blk = table[b * tbl_stride + pos / 64];
+  const int64_t dst = ((blk * Hkv + h) * 64 + pos % 64) * D + c * 8;
+  *reinterpret_cast<uint4*>(kp + dst) =
+      *reinterpret_cast<const uint4*>(k + b * k_sb + h * k_sh + s * k_ss + c * 8);
+  *reinterpret_cast<uint4*>(vp + dst) =
+      *reinterpret_cast<const uint4*>(v + b * v_sb + h * v_sh + s * v_ss + c * 8);
+}
+}  // namespace
+}  // namespace tpp
+
+extern "C" int tpp_kv_append_paged(const void* k, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                                   const void* v, int64_t v_sb, int64_t v_sh, int64_t v_ss,
+                                   void* k_pool, void* v_pool, int64_t num_blocks,
+                                   const int32_t* block_table, int64_t table_stride,
+                                   const int32_t* positions, int64_t start_pos, int64_t B,
+                                   int64_t Hkv, int64_t S, int64_t D, int dtype, void* stream) {
+  if (B * S == 0) return TPP_OK;
+  TPP_REQUIRE(k && v && k_pool && v_pool && block_table, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(B > 0 && Hkv > 0 && S > 0 && D > 0 && D % 8 == 0 && num_blocks > 0, TPP_ERR_SHAPE,
+              "bad sizes (D must be a multiple of 8)");
+  TPP_REQUIRE(k_sb % 8 == 0 && k_sh % 8 == 0 && k_ss % 8 == 0 && v_sb % 8 == 0 &&
+                  v_sh % 8 == 0 && v_ss % 8 == 0 && aligned16(k) && aligned16(v) &&
+                  aligned16(k_pool) && aligned16(v_pool),
+              TPP_ERR_ALIGN, "rows must be 16-byte aligned");
+  const int64_t total = B * Hkv * S * (D / 8);
+  return TPP_DISPATCH_HALF(dtype, T, [&] {
+    return launch("kv_append_paged_kernel", kv_append_paged_kernel<T>,
+                  dim3((unsigned)((total + 255) / 256)), dim3(256), 0, as_stream(stream), 0u,
+                  (const T*)k, k_sb, k_sh, k_ss, (const T*)v, v_sb, v_sh, v_ss, (T*)k_pool,
+                  (T*)v_pool, block_table, table_stride, Hkv, S, (int)D, start_pos, positions,
+                  total);
+  });
+}
+
 extern "C" int tpp_qk_norm_rope_cache(const void* qkv, int64_t ld_qkv, const void* qn_w,
                                       const void* kn_w, float eps, const void* cos,
                                       const void* sin, int64_t cs_stride, int cs_dtype,

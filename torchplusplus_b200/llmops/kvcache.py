@@ -72,3 +72,60 @@ class KVCache:
         if self.k_cache is not None:
             self.k_cache.zero_()
             self.v_cache.zero_()
+
+
+class PagedKVCache:
+    """Paged K/V storage for decode: block pools [num_blocks, Hkv, 64, D]
+    shared by all sequences, and a block table [batch, max_blocks] (int32,
+    on the device) mapping each sequence's 64-key blocks to pool blocks.
+    Blocks are handed out from a host-side free list, so sequences of very
+    different lengths share one pool instead of each reserving max_seq_len.
+    The reference lists a paged cache as a TODO (todo.md:8); the decode
+    kernels read it through tpp_attention_decode(_qkv)_paged."""
+
+    BLOCK = 64
+
+    def __init__(self, num_blocks: int, n_kv_heads: int, head_dim: int, dtype: torch.dtype,
+                 device, batch_size: int, max_seq_len: int):
+        self.k_pool = torch.zeros(num_blocks, n_kv_heads, self.BLOCK, head_dim, dtype=dtype,
+                                  device=device)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.max_blocks = (max_seq_len + self.BLOCK - 1) // self.BLOCK
+        self.block_table = torch.full((batch_size, self.max_blocks), -1, dtype=torch.int32,
+                                      device=device)
+        self._table = [[] for _ in range(batch_size)]  # host copy of each row
+        self._free = list(range(num_blocks))
+        self.max_seq_len = max_seq_len
+
+    @property
+    def free_blocks(self) -> int:
+        return len(self._free)
+
+    def reserve(self, b: int, length: int) -> None:
+        """Make sure sequence b owns blocks for positions < length."""
+        if length > self.max_seq_len:
+            raise ValueError("length exceeds max_seq_len")
+        need = (length + self.BLOCK - 1) // self.BLOCK - len(self._table[b])
+        if need <= 0:
+            return
+        if need > len(self._free):
+            raise RuntimeError("paged KV cache: out of blocks")
+        new = [self._free.pop() for _ in range(need)]
+        start = len(self._table[b])
+        self._table[b].extend(new)
+        self.block_table[b, start:start + need] = torch.tensor(new, dtype=torch.int32)
+
+    def release(self, b: int) -> None:
+        """Return sequence b's blocks to the pool."""
+        self._free.extend(reversed(self._table[b]))
+        self._table[b] = []
+        self.block_table[b].fill_(-1)
+
+    def append(self, k: torch.Tensor, v: torch.Tensor, start_pos: int = 0) -> None:
+        """k, v [B, Hkv, S, D] written at positions start_pos .. start_pos + S - 1."""
+        from .. import ops
+        B, _, S, _ = k.shape
+        for b in range(B):
+            self.reserve(b, start_pos + S)
+        ops.kv_append_paged(k, v, self.k_pool, self.v_pool, self.block_table,
+                            start_pos=start_pos)

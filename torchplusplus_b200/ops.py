@@ -409,6 +409,103 @@ def attention_decode_qkv(qkv: torch.Tensor, q_norm_w: torch.Tensor | None,
     return out
 
 
+def _paged_args(k_pool, v_pool, block_table, B):
+    NB, Hkv, blk, D = k_pool.shape
+    if blk != 64 or v_pool.shape != k_pool.shape or not k_pool.is_contiguous() \
+            or not v_pool.is_contiguous():
+        raise ValueError("pools must be contiguous [num_blocks, Hkv, 64, D]")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] != B \
+            or block_table.stride(1) != 1:
+        raise ValueError("block_table must be int32 [B, max_blocks] with unit column stride")
+    return NB, Hkv, D
+
+
+def attention_decode_paged(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                           block_table: torch.Tensor, seqlens: torch.Tensor, max_seqlen: int,
+                           window_left: int = -1, scale: float | None = None,
+                           out: torch.Tensor | None = None,
+                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """attention_decode over a paged cache: pools [num_blocks, Hkv, 64, D],
+    key k of sequence b in block block_table[b, k // 64], row k % 64."""
+    _cuda(q, k_pool, v_pool, block_table, seqlens)
+    dt = _half(q, "q")
+    _same_dtype(q, k_pool, v_pool)
+    B, Hq, D = q.shape
+    NB, Hkv, Dc = _paged_args(k_pool, v_pool, block_table, B)
+    if Dc != D or seqlens.dtype != torch.int32 or seqlens.numel() != B:
+        raise ValueError("head dims must match; seqlens int32 [B]")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+    need = decode_workspace_bytes(B, Hq, max_seqlen, D)
+    if workspace is None and need > 0:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    N.call("tpp_attention_decode_paged", q.data_ptr(), q.stride(0), q.stride(1),
+           k_pool.data_ptr(), v_pool.data_ptr(), NB, block_table.data_ptr(),
+           block_table.stride(0), seqlens.data_ptr(), int(max_seqlen), out.data_ptr(),
+           out.stride(0), out.stride(1), B, Hq, Hkv, D, int(window_left), float(scale),
+           N.ptr(workspace), 0 if workspace is None else workspace.numel(), dt, N.stream_of(q))
+    return out
+
+
+def attention_decode_qkv_paged(qkv: torch.Tensor, q_norm_w: torch.Tensor | None,
+                               k_norm_w: torch.Tensor | None, eps: float, cos: torch.Tensor,
+                               sin: torch.Tensor, positions: torch.Tensor, k_pool: torch.Tensor,
+                               v_pool: torch.Tensor, block_table: torch.Tensor,
+                               seqlens: torch.Tensor, max_seqlen: int, Hq: int, Hkv: int,
+                               window_left: int = -1, scale: float | None = None,
+                               out: torch.Tensor | None = None,
+                               workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """attention_decode_qkv over a paged cache (the new k/v rows are written
+    into the pools)."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, positions, k_pool, v_pool, block_table, seqlens)
+    dt = _half(qkv, "qkv")
+    _same_dtype(qkv, k_pool, v_pool, q_norm_w, k_norm_w)
+    B = qkv.shape[0]
+    NB, Hkv_p, D = _paged_args(k_pool, v_pool, block_table, B)
+    if Hkv_p != Hkv or qkv.shape[-1] != (Hq + 2 * Hkv) * D or qkv.stride(-1) != 1:
+        raise ValueError("qkv must be [B, 1, (Hq+2Hkv)*D] matching the pools")
+    for t, nm in ((positions, "positions"), (seqlens, "seqlens")):
+        if t.dtype != torch.int32 or t.numel() != B:
+            raise ValueError(f"{nm} must be int32 [B]")
+    cos, sin, cs_stride, cs_dt = _table(cos, sin, D)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=qkv.dtype, device=qkv.device)
+    need = decode_workspace_bytes(B, Hq, max_seqlen, D)
+    if workspace is None and need > 0:
+        workspace = torch.empty(need, dtype=torch.uint8, device=qkv.device)
+    N.call("tpp_attention_decode_qkv_paged", qkv.data_ptr(), qkv.stride(0), N.ptr(q_norm_w),
+           N.ptr(k_norm_w), float(eps), cos.data_ptr(), sin.data_ptr(), cs_stride, cs_dt,
+           positions.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), NB,
+           block_table.data_ptr(), block_table.stride(0), seqlens.data_ptr(), int(max_seqlen),
+           out.data_ptr(), out.stride(0), out.stride(1), B, Hq, Hkv, D, int(window_left),
+           float(scale), N.ptr(workspace), 0 if workspace is None else workspace.numel(), dt,
+           N.stream_of(qkv))
+    return out
+
+
+def kv_append_paged(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                    block_table: torch.Tensor, positions: torch.Tensor | None = None,
+                    start_pos: int = 0) -> None:
+    """k, v [B, Hkv, S, D] -> pools at positions (positions[b] or start_pos) + s."""
+    _cuda(k, v, k_pool, v_pool, block_table, positions)
+    dt = _half(k, "k")
+    _same_dtype(k, v, k_pool, v_pool)
+    B, Hkv, S, D = k.shape
+    NB, Hkv_p, Dp = _paged_args(k_pool, v_pool, block_table, B)
+    if v.shape != k.shape or Hkv_p != Hkv or Dp != D:
+        raise ValueError("k/v must be [B, Hkv, S, D] matching the pools")
+    if positions is not None and (positions.dtype != torch.int32 or positions.numel() != B):
+        raise ValueError("positions must be int32 [B]")
+    N.call("tpp_kv_append_paged", k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+           v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), k_pool.data_ptr(),
+           v_pool.data_ptr(), NB, block_table.data_ptr(), block_table.stride(0),
+           N.ptr(positions), int(start_pos), B, Hkv, S, D, dt, N.stream_of(k))
+
+
 # ---------------------------------------------------------------- cache / step helpers
 def qk_norm_rope_cache(qkv: torch.Tensor, q_norm_w: torch.Tensor | None,
                        k_norm_w: torch.Tensor | None, eps: float, cos: torch.Tensor,
