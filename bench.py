@@ -319,6 +319,19 @@ def per_op(hbm_peak: float, tc_peak: float) -> dict:
         t = _time_graph([lambda: ops.attention_decode(qd, kc, vc, sl, L, window_left=4095,
                                                       out=od, workspace=ws)] * 10) / 10
         rec(f"cfg5_swa_decode_B64_L{L}_w4096_bf16", t, nb, "GB/s")
+        if L == 4096:
+            # the same keys in a paged cache: 64-key blocks scattered over a pool
+            nblk = L // 64
+            perm = torch.randperm(B * nblk, device=dev)
+            table = perm.view(B, nblk).to(torch.int32)
+            kp = torch.empty(B * nblk, 8, 64, 128, dtype=torch.bfloat16, device=dev)
+            vp = torch.empty_like(kp)
+            ops.kv_append_paged(kc, vc, kp, vp, table, start_pos=0)
+            t = _time_graph([lambda: ops.attention_decode_paged(qd, kp, vp, table, sl, L,
+                                                                window_left=4095, out=od,
+                                                                workspace=ws)] * 10) / 10
+            rec(f"cfg5_swa_decode_paged_B64_L{L}_w4096_bf16", t, nb, "GB/s")
+            del kp, vp
         del kc, vc
     torch.cuda.synchronize()
     return res
