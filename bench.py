@@ -305,6 +305,17 @@ def per_op(hbm_peak: float, tc_peak: float) -> dict:
         rec(f"cfg3_linear_silu_M{M_}_K1024_N3072_f16", t, nb, "GB/s")
         del Ws
 
+    # on-device sampling of a decode step's logits (batch 32, Qwen3 vocabulary):
+    # algorithmic bytes = one read of the logits
+    lg = rnd(32, 151936, dtype=torch.bfloat16, std=3.0)
+    cnt = torch.arange(32, dtype=torch.int32, device=dev)
+    tok = torch.empty(32, dtype=torch.int64, device=dev)
+    t = _time_graph([lambda: ops.argmax(lg, out=tok)] * 10) / 10
+    rec("decode_argmax_B32_V151936_bf16", t, lg.numel() * 2, "GB/s")
+    t = _time_graph([lambda: ops.sample(lg, 0.8, 0, 0.9, 1, counters=cnt, out=tok)] * 10) / 10
+    rec("decode_sample_top_p0.9_B32_V151936_bf16", t, lg.numel() * 2, "GB/s")
+    del lg
+
     # config 5: sliding-window GQA decode, B64, Hq16/Hkv8, D128, window 4096, bf16
     for L in (1024, 4096, 16384, 32768):
         B = 64

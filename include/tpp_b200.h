@@ -163,6 +163,19 @@ int tpp_linear_packed(const void* x_packed, const void* w_packed, const void* bi
                       const void* residual, void* y, int64_t ldy, void* y_packed, int64_t M,
                       int64_t N, int64_t K, float eps, int act, int dtype, void* stream);
 
+/* One sampled token per row of logits [B, V] (row stride ld; V, ld multiples
+ * of 8): softmax(logits / temperature) restricted to the top_k largest
+ * logits (0 = no limit) and to the smallest descending prefix whose
+ * cumulative probability exceeds top_p (1 = no limit), the crossing token
+ * included -- LLMInference.sample_top_k / sample_top_p
+ * (torchpp/llmops/llm.py:114-203).  Tokens tied with a threshold are all
+ * kept.  The uniform draw is SplitMix64(seed, row, counters[row]) (counters
+ * may be NULL), so a CUDA graph replays with fresh randomness when the
+ * counters (e.g. positions) advance.  Greedy decoding: tpp_argmax. */
+int tpp_sample(const void* logits, int64_t ld, int64_t B, int64_t V, float temperature,
+               int64_t top_k, float top_p, uint64_t seed, const int32_t* counters, int64_t* out,
+               int dtype, void* stream);
+
 /* Bulk-prefetch [ptr, ptr + bytes) into L2 (16-byte aligned, bytes % 16 ==
  * 0); no data reaches the SMs.  Meant for a parallel branch of a decode
  * graph that warms the next layers' weights.  No reference counterpart. */

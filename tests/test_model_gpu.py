@@ -128,3 +128,33 @@ def test_torchpp_alias_runs_a_fastqwen3_style_block():
         z = lin(y)
     assert y.shape == (1, 8, 1024) and y2.shape == (1, 1, 1024) and z.shape == (1, 8, 3072)
     assert torch.isfinite(z).all() and cache.cache_len == 9
+
+
+def test_engine_sampling_generate():
+    """Non-greedy generate runs inside the decode graph: top-k 1 reproduces
+    the greedy sequence; top-p sampling stays in the vocabulary, varies with
+    the seed and is reproducible under torch.manual_seed."""
+    m = make(torch.bfloat16, seed=7)
+    ids = torch.randint(0, 1000, (3, 16), generator=torch.Generator().manual_seed(8))
+    with torch.inference_mode():
+        # top-k 1: every pick is a maximum of that step's logits (ties at the
+        # maximum are all kept, so the index may differ from argmax's first)
+        eng = m.engine(3, 40)
+        eng.set_sampling(temperature=0.8, top_k=1, seed=5)
+        eng.prefill(ids)
+        for _ in range(10):
+            eng.step_eager()
+            lg = eng.logits.float()
+            picked = lg.gather(1, eng.tokens[:, None])[:, 0]
+            assert torch.equal(picked, lg.max(dim=1).values)
+        eng.set_greedy()
+        torch.manual_seed(11)
+        a = m.generate(ids, max_new_token=12, sampling_strategy="top_p", top_p=0.9, temp=1.5).cpu()
+        torch.manual_seed(11)
+        b = m.generate(ids, max_new_token=12, sampling_strategy="top_p", top_p=0.9, temp=1.5).cpu()
+        torch.manual_seed(12)
+        c = m.generate(ids, max_new_token=12, sampling_strategy="top_p", top_p=0.9, temp=1.5).cpu()
+    assert a.shape == (3, 28) and torch.equal(a[:, :16], ids)
+    assert int(a.max()) < 1000 and int(a.min()) >= 0
+    assert torch.equal(a, b)
+    assert not torch.equal(a, c)

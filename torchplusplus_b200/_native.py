@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
                                   _i32, _p]),
     "tpp_hgemv": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
     "tpp_l2_prefetch": (_i32, [_p, _i64, _p]),
+    "tpp_sample": (_i32, [_p, _i64, _i64, _i64, _f32, _i64, _f32, C.c_uint64, _p, _p, _i32, _p]),
     "tpp_packed_weight_bytes": (_i64, [_i64, _i64, _i32]),
     "tpp_packed_activation_bytes": (_i64, [_i64, _i64]),
     "tpp_pack_weight": (_i32, [_p, _i64, _i64, _i32, _i32, _p, _p]),

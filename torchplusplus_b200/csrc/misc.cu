@@ -198,3 +198,249 @@ extern "C" int tpp_l2_prefetch(const void* ptr, int64_t bytes, void* stream) {
                                                                 bytes);
   return check_launch("l2_prefetch_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// On-device sampling: temperature + top-k + top-p (nucleus) + one draw per
+// row, the semantics of LLMInference.sample_top_k / sample_top_p
+// (torchpp/llmops/llm.py:114-203): softmax(logits / T) restricted to the k
+// largest logits and/or to the smallest descending prefix whose cumulative
+// probability exceeds p (the crossing token included).
+//
+// One CTA per row.  Thresholds come from an exact radix selection on the
+// 16-bit orderable keys of the logits (two passes of 256-bin histograms:
+// counts for top-k, probability mass for top-p), so tokens tied with the
+// threshold are all kept (torch's sort/topk keep an arbitrary subset of
+// such ties).  The draw is an inverse-CDF walk over the kept tokens in the
+// kernel's fixed visiting order with u from SplitMix64 (Steele, Lea & Flood,
+// OOPSLA 2014) of (seed, row, counter[row]) -- a different random stream
+// than torch.multinomial, the same distribution.
+// ---------------------------------------------------------------------------
+namespace tpp {
+namespace {
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t order_key(T v) {
+  const uint16_t h = *reinterpret_cast<const uint16_t*>(&v);
+  return (h & 0x8000u) ? (uint32_t)(~h & 0xFFFFu) : (uint32_t)(h | 0x8000u);
+}
+
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleWarps = kSampleThreads / 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(
+    const T* __restrict__ x, int64_t ld, int64_t V, float inv_temp_log2, int64_t top_k,
+    float top_p, uint64_t seed, const int32_t* __restrict__ counters, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ uint8_t sm_raw[];
+  uint32_t* hc = reinterpret_cast<uint32_t*>(sm_raw);                     // [warps][256]
+  float* hm = reinterpret_cast<float*>(hc + kSampleWarps * 256);         // [warps][256]
+  float* red = hm + kSampleWarps * 256;                                   // [warps]
+  __shared__ uint32_t s_key;
+  __shared__ float s_f[2];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x;
+  const T* row = x + (int64_t)b * ld;
+  const int64_t nv = V / 8;  // V % 8 == 0 (host)
+
+  auto block_max = [&](float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      v = lane < kSampleWarps ? red[lane] : -INFINITY;
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) s_f[0] = v;
+    }
+    __syncthreads();
+    const float r = s_f[0];
+    __syncthreads();
+    return r;
+  };
+  auto for_row = [&](auto&& f) {  // f(key, value, index) over the whole row
+    for (int64_t c = tid; c < nv; c += kSampleThreads) {
+      const uint4 u = ldg_nc_v4(row + c * 8);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f(order_key<T>(e[j]), to_f32(e[j]), c * 8 + j);
+    }
+  };
+
+  // 1. row max (softmax stabiliser) and its first index (the fallback pick)
+  float mx = -INFINITY;
+  int64_t mi = V;
+  for_row([&](uint32_t, float v, int64_t i) {
+    if (v > mx || (v == mx && i < mi)) { mx = v; mi = i; }
+  });
+  __shared__ long long s_arg;
+  if (tid == 0) s_arg = V;
+  const float rmx = block_max(mx);
+  if (mx == rmx) atomicMin(&s_arg, (long long)mi);
+  mx = rmx;
+  auto weight = [&](float v) { return exp2f((v - mx) * inv_temp_log2); };
+
+  // radix selection helpers: per-warp histograms, then a descending scan
+  auto clear = [&]() {
+    for (int i = tid; i < kSampleWarps * 256; i += kSampleThreads) { hc[i] = 0u; hm[i] = 0.f; }
+    __syncthreads();
+  };
+  // descending scan of the (summed) bins: first bin from the top whose
+  // cumulative total reaches `target` (counts: >=, mass: >); returns the bin
+  // and writes the total above it to s_f[1]
+  auto pick_bin = [&](bool mass, float target) -> uint32_t {
+    if (tid < 256) {
+      float c = 0.f;
+      for (int w = 0; w < kSampleWarps; ++w)
+        c += mass ? hm[w * 256 + tid] : (float)hc[w * 256 + tid];
+      hm[tid] = c;  // warp 0's row now holds the totals
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float above = 0.f;
+      uint32_t bin = 0;
+      for (int i = 255; i >= 0; --i) {
+        const float c = hm[i];
+        const bool hit = mass ? (above + c > target) : (above + c >= target);
+        if (hit) { bin = (uint32_t)i; break; }
+        above += c;
+      }
+      s_key = bin;
+      s_f[1] = above;
+    }
+    __syncthreads();
+    return s_key;
+  };
+
+  // 2. top-k threshold on the keys
+  uint32_t tk = 0;
+  if (top_k > 0 && top_k < V) {
+    clear();
+    for_row([&](uint32_t k, float, int64_t) { atomicAdd(&hc[warp * 256 + (k >> 8)], 1u); });
+    __syncthreads();
+    const uint32_t hb = pick_bin(false, (float)top_k);
+    const float above = s_f[1];
+    __syncthreads();
+    clear();
+    for_row([&](uint32_t k, float, int64_t) {
+      if ((k >> 8) == hb) atomicAdd(&hc[warp * 256 + (k & 255u)], 1u);
+    });
+    __syncthreads();
+    const uint32_t lb = pick_bin(false, (float)top_k - above);
+    tk = (hb << 8) | lb;
+  }
+  // 3. top-p threshold among the kept keys, by probability mass
+  uint32_t t = tk;
+  if (top_p < 1.f) {
+    clear();
+    for_row([&](uint32_t k, float v, int64_t) {
+      if (k >= tk) atomicAdd(&hm[warp * 256 + (k >> 8)], weight(v));
+    });
+    __syncthreads();
+    // total mass Z first (the bins sum to it)
+    if (tid < 256) {
+      float c = 0.f;
+      for (int w = 0; w < kSampleWarps; ++w) c += hm[w * 256 + tid];
+      hc[tid] = __float_as_uint(c);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float z = 0.f;
+      for (int i = 0; i < 256; ++i) z += __uint_as_float(hc[i]);
+      s_f[0] = z;
+    }
+    __syncthreads();
+    const float target = top_p * s_f[0];
+    const uint32_t hb = pick_bin(true, target);
+    const float above = s_f[1];
+    __syncthreads();
+    clear();
+    for_row([&](uint32_t k, float v, int64_t) {
+      if (k >= tk && (k >> 8) == hb) atomicAdd(&hm[warp * 256 + (k & 255u)], weight(v));
+    });
+    __syncthreads();
+    const uint32_t lb = pick_bin(true, target - above);
+    const uint32_t tp = (hb << 8) | lb;
+    t = tp > tk ? tp : tk;
+  }
+  // 4. inverse-CDF draw over kept tokens (key >= t), fixed visiting order
+  float part = 0.f;
+  for_row([&](uint32_t k, float v, int64_t) { if (k >= t) part += weight(v); });
+  // inclusive block scan of the per-thread partial sums
+  float incl = part;
+  for (int o = 1; o < 32; o <<= 1) {
+    const float n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < kSampleWarps ? red[lane] : 0.f;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    if (lane < kSampleWarps) red[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const float before_warp = warp > 0 ? red[warp - 1] : 0.f;
+  const float total = red[kSampleWarps - 1];
+  const float excl = before_warp + incl - part;
+  const uint64_t r = splitmix64(seed ^ ((uint64_t)b * 0xD1B54A32D192ED03ull) ^
+                                ((uint64_t)(counters ? counters[b] : 0) << 32));
+  const float u = (float)(r >> 40) * (1.0f / 16777216.0f) * total;
+  __shared__ long long s_pick;
+  if (tid == 0) s_pick = -1;
+  __syncthreads();
+  // the thread whose range holds u walks its elements again (same order and
+  // arithmetic as `part`, so its running sum reproduces excl .. excl + part)
+  if (part > 0.f && u >= excl && (u < excl + part || tid == kSampleThreads - 1 ||
+                                   excl + part >= total)) {
+    float run = excl;
+    int64_t last = -1, pick = -1;
+    for_row([&](uint32_t k, float v, int64_t i) {
+      if (k >= t && pick < 0) {
+        run += weight(v);
+        last = i;
+        if (run > u) pick = i;
+      }
+    });
+    atomicMax(&s_pick, (long long)(pick >= 0 ? pick : last));
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // u fell between two threads' ranges through rounding: take the row max
+    const long long pk = s_pick >= 0 ? s_pick : s_arg;
+    out[b] = pk;
+  }
+}
+}  // namespace
+}  // namespace tpp
+
+extern "C" int tpp_sample(const void* logits, int64_t ld, int64_t B, int64_t V, float temperature,
+                          int64_t top_k, float top_p, uint64_t seed, const int32_t* counters,
+                          int64_t* out, int dtype, void* stream) {
+  if (B == 0) return TPP_OK;
+  TPP_REQUIRE(logits && out, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(B > 0 && V > 0 && ld >= V && V % 8 == 0 && ld % 8 == 0, TPP_ERR_SHAPE,
+              "need V and the row stride multiples of 8");
+  TPP_REQUIRE(aligned16(logits), TPP_ERR_ALIGN, "logits must be 16-byte aligned");
+  TPP_REQUIRE(temperature > 0.f && top_p > 0.f && top_k >= 0, TPP_ERR_SHAPE,
+              "need temperature > 0, top_p > 0, top_k >= 0 (greedy: tpp_argmax)");
+  const size_t smem = (size_t)kSampleWarps * 256 * 8 + kSampleWarps * 4;
+  const float itl = 1.4426950408889634f / temperature;
+  return TPP_DISPATCH_HALF(dtype, T, [&] {
+    cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    return launch("sample_kernel", sample_kernel<T>, dim3((unsigned)B), dim3(kSampleThreads),
+                  smem, as_stream(stream), 0u, (const T*)logits, ld, V, itl, top_k, top_p,
+                  seed, counters, out);
+  });
+}

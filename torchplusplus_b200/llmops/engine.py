@@ -111,6 +111,9 @@ class DecodeEngine:
         # batch 32 -- the fork costs the chain its programmatic launch edge
         # and the prefetches compete with the K/V stream).
         self.l2_warm = False
+        # None = greedy; else dict(temperature, top_k, top_p, seed) (set_sampling)
+        self.sampling: Optional[dict] = None
+        self._graph_sampling: Optional[dict] = None
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step: int | None = None
         self.prompt_len = 0
@@ -146,12 +149,33 @@ class DecodeEngine:
             ops.rmsnorm_linear(x, L["wgu_f"], self.eps, act="swiglu", out=ln["ff"])
             ops.linear(ln["ff"], L["wdown"], residual=x, out=x)
         ops.rmsnorm_linear(x, self.lm_head_f, self.eps, out=ln["logits"])
-        ops.argmax(ln["logits"], out=ln["tokens"])
+        self._pick(ln["logits"], ln["positions"], ln["tokens"])
         ops.decode_advance(ln["tokens"], ln["out_ids"], ln["positions"], ln["seqlens"])
+
+    def _pick(self, logits: torch.Tensor, counters: torch.Tensor, out: torch.Tensor) -> None:
+        """Next token per row: argmax, or an on-device draw (temperature /
+        top-k / top-p) keyed by the row's position, so each graph replay
+        draws afresh."""
+        if self.sampling is None:
+            ops.argmax(logits, out=out)
+        else:
+            sp = self.sampling
+            ops.sample(logits, sp["temperature"], sp["top_k"], sp["top_p"], sp["seed"],
+                       counters=counters, out=out)
 
     def _step(self) -> None:
         for ln in self.lanes:
             self._step_lane(ln)
+
+    def set_sampling(self, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+                     seed: int = 0) -> None:
+        """Sample instead of argmax (None-equivalent: set_greedy).  The decode
+        graph is re-recorded when the setting changes."""
+        self.sampling = dict(temperature=float(temperature), top_k=int(top_k),
+                             top_p=float(top_p), seed=int(seed))
+
+    def set_greedy(self) -> None:
+        self.sampling = None
 
     def step_eager(self) -> None:
         """One decode step launched directly (no graph); used by tests."""
@@ -186,6 +210,7 @@ class DecodeEngine:
             self.launches_per_step = N.launch_count() - n0
         torch.cuda.current_stream(self.device).wait_stream(main)
         self.graph = g
+        self._graph_sampling = None if self.sampling is None else dict(self.sampling)
 
     # ------------------------------------------------------------ prefill
     @torch.inference_mode()
@@ -203,7 +228,8 @@ class DecodeEngine:
             x = blk(x, self.cos, self.sin, c, 0)
         h = ops.rmsnorm(x[:, -1], self.nf, self.eps)
         ops.linear(h, self.lm_head, out=self.logits)
-        ops.argmax(self.logits, out=self.tokens)
+        self._pick(self.logits, torch.full((B,), S - 1, dtype=torch.int32, device=self.device),
+                   self.tokens)
         self.out_ids[:, :S].copy_(ids)
         self.out_ids[:, S].copy_(self.tokens)
         self.positions.fill_(S)
@@ -211,7 +237,7 @@ class DecodeEngine:
         self.prompt_len = S
 
     def decode(self, steps: int) -> None:
-        if self.graph is None:
+        if self.graph is None or self._graph_sampling != self.sampling:
             self.capture()
         for _ in range(steps):
             self.graph.replay()

@@ -149,11 +149,22 @@ class Qwen3(LLMInference):
                  top_p: float = 0.9, top_k: Optional[int] = None,
                  sampling_strategy: str = "top_p", stop_token_ids=None, eos_token_id=None,
                  stream: bool = False, stream_callback=None):
-        if sampling_strategy != "greedy" or stream:
+        if stream or sampling_strategy not in ("greedy", "top_p", "top_k") or \
+                (sampling_strategy == "top_k" and top_k is None):
             return super().generate(input_ids, max_new_token, temp, top_p, top_k,
                                     sampling_strategy, stop_token_ids, eos_token_id, stream,
                                     stream_callback)
         B, S = input_ids.shape
         eng = self.engine(B, S + max_new_token)
+        if sampling_strategy == "greedy":
+            eng.set_greedy()
+        else:
+            # the reference's strategies are exclusive (llm.py:107-116); the
+            # draw seed comes from torch's generator, so torch.manual_seed
+            # makes a run reproducible
+            eng.set_sampling(temperature=temp,
+                             top_k=top_k if sampling_strategy == "top_k" else 0,
+                             top_p=top_p if sampling_strategy == "top_p" else 1.0,
+                             seed=int(torch.randint(0, 2 ** 62, (1,)).item()))
         return eng.generate(input_ids, max_new_token, eos_token_id=eos_token_id,
                             stop_token_ids=stop_token_ids)

@@ -564,6 +564,27 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     return out
 
 
+def sample(logits: torch.Tensor, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
+           seed: int = 0, counters: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """One token per row of logits [B, V] from softmax(logits / temperature)
+    restricted to the top_k largest logits and the top_p nucleus, on the
+    device (see tpp_sample).  counters (int32 [B], e.g. positions) select the
+    random draw per row."""
+    _cuda(logits, counters)
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    B, V = logits.shape
+    if counters is not None and (counters.dtype != torch.int32 or counters.numel() != B):
+        raise ValueError("counters must be int32 [B]")
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=logits.device)
+    N.call("tpp_sample", logits.data_ptr(), logits.stride(0), B, V, float(temperature),
+           int(top_k), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF, N.ptr(counters),
+           out.data_ptr(), N.dtype_code(logits.dtype), N.stream_of(logits))
+    return out
+
+
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _cuda(ids, table)
     dt = _half(table, "table")
