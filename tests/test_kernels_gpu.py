@@ -447,5 +447,26 @@ def test_argmax_and_embedding():
     assert torch.equal(emb, table[ids])
 
 
+@pytest.mark.parametrize("V,ld,dtype", [(5, 5, torch.bfloat16), (37, 40, torch.float16),
+                                         (64, 64, torch.bfloat16), (1003, 1003, torch.float16),
+                                         (151936, 151936, torch.float32),
+                                         (151937, 151944, torch.bfloat16)])
+def test_argmax_row_slices(V, ld, dtype):
+    """Rows are split over a CTA cluster: ties across slices resolve to the
+    first index, NaN wins, a maximum in the vector tail is found."""
+    g = gen(31)
+    base = rnd(6, ld, g=g, dtype=dtype)
+    logits = base[:, :V]
+    logits[1, V - 1] = 50.0                  # max in the last element (tail)
+    logits[2, V // 2] = 50.0
+    logits[2, V - 1] = 50.0                  # tie across slices -> first
+    logits[3].fill_(-1.0)                    # all equal -> 0
+    logits[4, V // 3] = float("nan")         # NaN is the max
+    logits[5, 0] = 50.0
+    logits[5, V - 1] = 50.0
+    got = ops.argmax(base.to(DEV)[:, :V]).cpu()
+    assert torch.equal(got, torch.argmax(logits.float(), dim=-1))
+
+
 def test_no_bounded_wait_expired():
     assert ops.device_error() == 0

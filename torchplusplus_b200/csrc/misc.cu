@@ -8,20 +8,58 @@
 namespace tpp {
 namespace {
 
-// One CTA per row.  Ties resolve to the smallest index, like torch.argmax.
+// Rows are split over a cluster of kRowCtas CTAs (one slice each); the
+// slices' partial results meet through distributed shared memory, so a batch
+// of 32 rows fills 256 SMs' worth of CTAs instead of 32.
+constexpr int kRowCtas = 8;
+constexpr int kRowThreads = 512;
+constexpr int kRowWarps = kRowThreads / 32;
+
+__device__ __forceinline__ uint32_t cl_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// full cluster barrier: this CTA's shared-memory writes are visible to the
+// peers' reads after it
+__device__ __forceinline__ void cl_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_peer_f32(const float* p, uint32_t rank) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(peer_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ long long ld_peer_s64(const long long* p, uint32_t rank) {
+  long long v;
+  asm volatile("ld.shared::cluster.s64 %0, [%1];" : "=l"(v) : "r"(peer_addr(p, rank)) : "memory");
+  return v;
+}
+
+// One cluster per row.  Ties resolve to the smallest index, like torch.argmax.
 // NaN compares greater than everything (torch.argmax treats NaN as the max).
 template <typename T>
-__global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, int64_t ld,
-                                                      int64_t V, int64_t* __restrict__ out,
-                                                      bool vec) {
+__global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T* __restrict__ x, int64_t ld,
+                                                             int64_t V, int64_t* __restrict__ out,
+                                                             bool vec) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float sv[32];
-  __shared__ int64_t si[32];
+  __shared__ float sv[kRowWarps];
+  __shared__ long long si[kRowWarps];
+  __shared__ float c_v;
+  __shared__ long long c_i;
+  const uint32_t cr = cl_rank();
   const T* row = x + (int64_t)blockIdx.x * ld;
   float best = -INFINITY;
-  int64_t bi = V;  // sentinel larger than any index
-  auto take = [&](float v, int64_t i) {
+  long long bi = V;  // sentinel larger than any index
+  auto take = [&](float v, long long i) {
     const bool vn = isnan(v), bn = isnan(best);
     if ((vn && !bn) || (!bn && v > best) || ((v == best || (vn && bn)) && i < bi)) {
       best = v;
@@ -29,13 +67,14 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, i
     }
   };
   if (vec) {
-    const int64_t nv = V / 8;
-    const int64_t step = blockDim.x;
-    int64_t c = threadIdx.x;
+    const int64_t nv = V / 8, per = (nv + kRowCtas - 1) / kRowCtas;
+    const int64_t c0 = (int64_t)cr * per, c1 = c0 + per < nv ? c0 + per : nv;
+    constexpr int step = kRowThreads;
+    int64_t c = c0 + threadIdx.x;
     // four independent 16-byte loads in flight per thread (the logits were
     // just written: each round trip is an L2 latency); order does not matter,
     // ties are resolved by index
-    for (; c + 3 * step < nv; c += 4 * step) {
+    for (; c + 3 * step < c1; c += 4 * step) {
       uint4 u[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) u[q] = ldg_nc_v4(row + (c + q * step) * 8);
@@ -47,37 +86,45 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ x, i
         for (int j = 0; j < 8; ++j) take(f[j], (c + q * step) * 8 + j);
       }
     }
-    for (; c < nv; c += step) {
+    for (; c < c1; c += step) {
       float f[8];
       unpack8<T>(ldg_nc_v4(row + c * 8), f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) take(f[j], c * 8 + j);
     }
-    for (int64_t i = nv * 8 + threadIdx.x; i < V; i += blockDim.x) take(to_f32(row[i]), i);
+    if (cr == kRowCtas - 1)
+      for (int64_t i = nv * 8 + threadIdx.x; i < V; i += kRowThreads) take(to_f32(row[i]), i);
   } else {
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) take(to_f32(row[i]), i);
+    const int64_t per = (V + kRowCtas - 1) / kRowCtas;
+    const int64_t i0 = (int64_t)cr * per, i1 = i0 + per < V ? i0 + per : V;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += kRowThreads) take(to_f32(row[i]), i);
   }
+  auto warp_take = [&]() {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    take(ov, oi);
-  }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const long long oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      take(ov, oi);
+    }
+  };
+  warp_take();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) { sv[warp] = best; si[warp] = bi; }
   __syncthreads();
   if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    best = lane < nw ? sv[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : V;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      take(ov, oi);
-    }
+    best = lane < kRowWarps ? sv[lane] : -INFINITY;
+    bi = lane < kRowWarps ? si[lane] : V;
+    warp_take();
+    if (lane == 0) { c_v = best; c_i = bi; }
+  }
+  cl_sync();
+  if (cr == 0 && warp == 0) {
+    best = lane < kRowCtas ? ld_peer_f32(&c_v, lane) : -INFINITY;
+    bi = lane < kRowCtas ? ld_peer_s64(&c_i, lane) : V;
+    warp_take();
     if (lane == 0) out[blockIdx.x] = bi < V ? bi : 0;
   }
+  cl_sync();  // the peers' shared memory stays live until rank 0 has read it
 }
 
 template <typename T>
@@ -138,14 +185,16 @@ extern "C" int tpp_argmax(const void* logits, int64_t ld, int64_t B, int64_t V, 
   auto go = [&](auto tag) -> int {
     using T = decltype(tag);
     const bool vec = (ld % 8 == 0) && aligned16(logits) && sizeof(T) == 2;
-    return launch("argmax_kernel", argmax_kernel<T>, dim3((unsigned)B), dim3(1024), 0, as_stream(stream), 0, (const T*)logits, ld, V, out,
-                                                                  vec);
+    return launch("argmax_kernel", argmax_kernel<T>, dim3((unsigned)B, kRowCtas),
+                  dim3(kRowThreads), 0, as_stream(stream), (unsigned)kRowCtas,
+                  (const T*)logits, ld, V, out, vec);
   };
   if (dtype == TPP_F16) return go(__half());
   if (dtype == TPP_BF16) return go(__nv_bfloat16());
   if (dtype == TPP_F32) {
-    return launch("argmax_kernel", argmax_kernel<float>, dim3((unsigned)B), dim3(1024), 0, as_stream(stream), 0, (const float*)logits, ld, V,
-                                                                      out, false);
+    return launch("argmax_kernel", argmax_kernel<float>, dim3((unsigned)B, kRowCtas),
+                  dim3(kRowThreads), 0, as_stream(stream), (unsigned)kRowCtas,
+                  (const float*)logits, ld, V, out, false);
   }
   set_error("tpp_argmax: dtype must be f16, bf16 or f32");
   return TPP_ERR_DTYPE;
@@ -206,14 +255,20 @@ extern "C" int tpp_l2_prefetch(const void* ptr, int64_t bytes, void* stream) {
 // largest logits and/or to the smallest descending prefix whose cumulative
 // probability exceeds p (the crossing token included).
 //
-// One CTA per row.  Thresholds come from an exact radix selection on the
-// 16-bit orderable keys of the logits (two passes of 256-bin histograms:
-// counts for top-k, probability mass for top-p), so tokens tied with the
-// threshold are all kept (torch's sort/topk keep an arbitrary subset of
-// such ties).  The draw is an inverse-CDF walk over the kept tokens in the
-// kernel's fixed visiting order with u from SplitMix64 (Steele, Lea & Flood,
-// OOPSLA 2014) of (seed, row, counter[row]) -- a different random stream
-// than torch.multinomial, the same distribution.
+// One cluster of kRowCtas CTAs per row; each CTA stages its slice of the
+// row in shared memory once and every later pass reads it from there.
+// Thresholds come from an exact radix selection on the 16-bit orderable keys
+// of the logits (two passes of 256-bin histograms: counts for top-k,
+// probability mass for top-p), so tokens tied with the threshold are all
+// kept (torch's sort/topk keep an arbitrary subset of such ties).  The
+// histograms are lane-replicated ([bin][lane]) so the many logits that share
+// a high byte do not serialise a warp's shared-memory atomics; the slices'
+// bin totals are summed through distributed shared memory, in the same
+// order in every CTA, so all CTAs pick the same thresholds.  The draw is an
+// inverse-CDF walk over the kept tokens in a fixed visiting order (slices in
+// rank order, threads in index order) with u from SplitMix64 (Steele, Lea &
+// Flood, OOPSLA 2014) of (seed, row, counter[row]) -- a different random
+// stream than torch.multinomial, the same distribution.
 // ---------------------------------------------------------------------------
 namespace tpp {
 namespace {
@@ -231,194 +286,297 @@ __device__ __forceinline__ uint32_t order_key(T v) {
   return (h & 0x8000u) ? (uint32_t)(~h & 0xFFFFu) : (uint32_t)(h | 0x8000u);
 }
 
-constexpr int kSampleThreads = 1024;
-constexpr int kSampleWarps = kSampleThreads / 32;
+// dynamic shared memory of the sampling kernel: histogram [256][32] words,
+// two merge buffers [2][256], the cluster totals [256], then the staged slice
+// (16-byte vectors) when it fits
+constexpr int kHistWords = 256 * 32;
+constexpr size_t kSampleFixedSmem = (size_t)(kHistWords + 3 * 256) * 4;
 
 template <typename T>
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(
+__global__ void __launch_bounds__(kRowThreads) sample_kernel(
     const T* __restrict__ x, int64_t ld, int64_t V, float inv_temp_log2, int64_t top_k,
-    float top_p, uint64_t seed, const int32_t* __restrict__ counters, int64_t* __restrict__ out) {
+    float top_p, uint64_t seed, const int32_t* __restrict__ counters, int64_t* __restrict__ out,
+    bool staged) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ uint8_t sm_raw[];
-  uint32_t* hc = reinterpret_cast<uint32_t*>(sm_raw);                     // [warps][256]
-  float* hm = reinterpret_cast<float*>(hc + kSampleWarps * 256);         // [warps][256]
-  float* red = hm + kSampleWarps * 256;                                   // [warps]
-  __shared__ uint32_t s_key;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(sm_raw);           // [256][32]
+  float* mbuf = reinterpret_cast<float*>(hist + kHistWords);      // [2][256]
+  float* gtot = mbuf + 2 * 256;                                    // [256]
+  uint4* slice = reinterpret_cast<uint4*>(gtot + 256);
+  __shared__ float red[kRowWarps];
+  __shared__ long long redi[kRowWarps];
   __shared__ float s_f[2];
+  __shared__ uint32_t s_bin;
+  __shared__ long long s_arg, s_pick;
+  __shared__ int s_owner;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t cr = cl_rank();
   const int b = blockIdx.x;
   const T* row = x + (int64_t)b * ld;
   const int64_t nv = V / 8;  // V % 8 == 0 (host)
+  const int64_t per = (nv + kRowCtas - 1) / kRowCtas;
+  const int64_t c0 = (int64_t)cr * per;
+  const int n = (int)(c0 >= nv ? 0 : (nv - c0 < per ? nv - c0 : per));
+  int mb = 0;  // merge buffer in use
 
-  auto block_max = [&](float v) {
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-      v = lane < kSampleWarps ? red[lane] : -INFINITY;
-      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (lane == 0) s_f[0] = v;
+  // sums a 256-entry per-CTA array over the cluster into gtot (rank order)
+  auto merge = [&](const float* mine) {
+    cl_sync();
+    if (tid < 256) {
+      float t = 0.f;
+#pragma unroll
+      for (int r = 0; r < kRowCtas; ++r) t += ld_peer_f32(mine + tid, r);
+      gtot[tid] = t;
     }
     __syncthreads();
-    const float r = s_f[0];
-    __syncthreads();
-    return r;
   };
-  auto for_row = [&](auto&& f) {  // f(key, value, index) over the whole row
-    for (int64_t c = tid; c < nv; c += kSampleThreads) {
-      const uint4 u = ldg_nc_v4(row + c * 8);
+  auto for_slice = [&](auto&& f) {  // f(key, value, index) over this CTA's slice
+    for (int c = tid; c < n; c += kRowThreads) {
+      const uint4 u = staged ? slice[c] : ldg_nc_v4(row + (c0 + c) * 8);
       const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f(order_key<T>(e[j]), to_f32(e[j]), c * 8 + j);
+      for (int j = 0; j < 8; ++j) f(order_key<T>(e[j]), to_f32(e[j]), (c0 + c) * 8 + j);
     }
   };
 
-  // 1. row max (softmax stabiliser) and its first index (the fallback pick)
+  // 1. stage the slice; row max (softmax stabiliser) and its first index
   float mx = -INFINITY;
-  int64_t mi = V;
-  for_row([&](uint32_t, float v, int64_t i) {
+  long long mi = V;
+  auto take = [&](float v, long long i) {
     if (v > mx || (v == mx && i < mi)) { mx = v; mi = i; }
-  });
-  __shared__ long long s_arg;
-  if (tid == 0) s_arg = V;
-  const float rmx = block_max(mx);
-  if (mx == rmx) atomicMin(&s_arg, (long long)mi);
-  mx = rmx;
+  };
+  {
+    int c = tid;
+    for (; c + 3 * kRowThreads < n; c += 4 * kRowThreads) {
+      uint4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u[q] = ldg_nc_v4(row + (c0 + c + q * kRowThreads) * 8);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (staged) slice[c + q * kRowThreads] = u[q];
+        const T* e = reinterpret_cast<const T*>(&u[q]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) take(to_f32(e[j]), (c0 + c + q * kRowThreads) * 8 + j);
+      }
+    }
+    for (; c < n; c += kRowThreads) {
+      const uint4 u = ldg_nc_v4(row + (c0 + c) * 8);
+      if (staged) slice[c] = u;
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) take(to_f32(e[j]), (c0 + c) * 8 + j);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
+    const long long oi = __shfl_xor_sync(0xffffffffu, mi, o);
+    take(ov, oi);
+  }
+  if (lane == 0) { red[warp] = mx; redi[warp] = mi; }
+  __syncthreads();
+  if (warp == 0) {
+    mx = lane < kRowWarps ? red[lane] : -INFINITY;
+    mi = lane < kRowWarps ? redi[lane] : V;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
+      const long long oi = __shfl_xor_sync(0xffffffffu, mi, o);
+      take(ov, oi);
+    }
+    if (lane == 0) {
+      mbuf[0] = mx;
+      reinterpret_cast<long long*>(mbuf)[1] = mi;  // words 2..3
+    }
+  }
+  cl_sync();
+  if (warp == 0) {
+    mx = lane < kRowCtas ? ld_peer_f32(mbuf, lane) : -INFINITY;
+    mi = lane < kRowCtas ? ld_peer_s64(reinterpret_cast<const long long*>(mbuf) + 1, lane) : V;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
+      const long long oi = __shfl_xor_sync(0xffffffffu, mi, o);
+      take(ov, oi);
+    }
+    if (lane == 0) { s_f[0] = mx; s_arg = mi < V ? mi : 0; }
+  }
+  __syncthreads();
+  mx = s_f[0];
+  mb = 1;
   auto weight = [&](float v) { return exp2f((v - mx) * inv_temp_log2); };
 
-  // radix selection helpers: per-warp histograms, then a descending scan
+  // radix selection helpers
   auto clear = [&]() {
-    for (int i = tid; i < kSampleWarps * 256; i += kSampleThreads) { hc[i] = 0u; hm[i] = 0.f; }
+    uint4* h4 = reinterpret_cast<uint4*>(hist);
+    for (int i = tid; i < kHistWords / 4; i += kRowThreads) h4[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
   };
-  // descending scan of the (summed) bins: first bin from the top whose
-  // cumulative total reaches `target` (counts: >=, mass: >); returns the bin
-  // and writes the total above it to s_f[1]
-  auto pick_bin = [&](bool mass, float target) -> uint32_t {
+  // folds the lane copies into this CTA's 256 totals, then sums the cluster
+  auto fold_merge = [&](bool mass) {
+    __syncthreads();
+    float* mine = mbuf + mb * 256;
     if (tid < 256) {
-      float c = 0.f;
-      for (int w = 0; w < kSampleWarps; ++w)
-        c += mass ? hm[w * 256 + tid] : (float)hc[w * 256 + tid];
-      hm[tid] = c;  // warp 0's row now holds the totals
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float above = 0.f;
-      uint32_t bin = 0;
-      for (int i = 255; i >= 0; --i) {
-        const float c = hm[i];
-        const bool hit = mass ? (above + c > target) : (above + c >= target);
-        if (hit) { bin = (uint32_t)i; break; }
-        above += c;
+      float t = 0.f;
+      for (int l = 0; l < 32; ++l) {
+        const uint32_t w = hist[tid * 32 + ((l + tid) & 31)];
+        t += mass ? __uint_as_float(w) : (float)w;
       }
-      s_key = bin;
-      s_f[1] = above;
+      mine[tid] = t;
+    }
+    merge(mine);
+    mb ^= 1;
+  };
+  // descending scan of gtot: the first bin from the top whose cumulative
+  // total reaches `target` (counts: >=, mass: >); target = frac * total when
+  // frac >= 0.  Writes the total above that bin to s_f[1]; with no such bin
+  // (rounding), bin 0 and the whole total.
+  auto pick_bin = [&](bool mass, float target, float frac) -> uint32_t {
+    if (warp == 0) {
+      float c[8], own = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { c[j] = gtot[lane * 8 + j]; own += c[j]; }
+      float suf = own;  // sum over lanes >= this lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float nb = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += nb;
+      }
+      const float total = __shfl_sync(0xffffffffu, suf, 0);
+      if (frac >= 0.f) target = frac * total;
+      float above = suf - own;
+      int hit = -1;
+      float hit_above = 0.f;
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {
+        const bool h = mass ? (above + c[j] > target) : (above + c[j] >= target);
+        if (h && hit < 0) { hit = j; hit_above = above; }
+        above += c[j];
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, hit >= 0);
+      if (bal == 0u) {
+        if (lane == 0) { s_bin = 0u; s_f[1] = total; s_f[0] = target; }
+      } else {
+        const int hl = 31 - __clz(bal);
+        if (lane == hl) { s_bin = (uint32_t)(lane * 8 + hit); s_f[1] = hit_above; s_f[0] = target; }
+      }
     }
     __syncthreads();
-    return s_key;
+    return s_bin;
   };
 
   // 2. top-k threshold on the keys
   uint32_t tk = 0;
   if (top_k > 0 && top_k < V) {
     clear();
-    for_row([&](uint32_t k, float, int64_t) { atomicAdd(&hc[warp * 256 + (k >> 8)], 1u); });
-    __syncthreads();
-    const uint32_t hb = pick_bin(false, (float)top_k);
+    for_slice([&](uint32_t k, float, int64_t) { atomicAdd(&hist[(k >> 8) * 32 + lane], 1u); });
+    fold_merge(false);
+    const uint32_t hb = pick_bin(false, (float)top_k, -1.f);
     const float above = s_f[1];
-    __syncthreads();
     clear();
-    for_row([&](uint32_t k, float, int64_t) {
-      if ((k >> 8) == hb) atomicAdd(&hc[warp * 256 + (k & 255u)], 1u);
+    for_slice([&](uint32_t k, float, int64_t) {
+      if ((k >> 8) == hb) atomicAdd(&hist[(k & 255u) * 32 + lane], 1u);
     });
-    __syncthreads();
-    const uint32_t lb = pick_bin(false, (float)top_k - above);
+    fold_merge(false);
+    const uint32_t lb = pick_bin(false, (float)top_k - above, -1.f);
     tk = (hb << 8) | lb;
   }
   // 3. top-p threshold among the kept keys, by probability mass
   uint32_t t = tk;
   if (top_p < 1.f) {
+    float* hm = reinterpret_cast<float*>(hist);
     clear();
-    for_row([&](uint32_t k, float v, int64_t) {
-      if (k >= tk) atomicAdd(&hm[warp * 256 + (k >> 8)], weight(v));
+    for_slice([&](uint32_t k, float v, int64_t) {
+      if (k >= tk) atomicAdd(&hm[(k >> 8) * 32 + lane], weight(v));
     });
-    __syncthreads();
-    // total mass Z first (the bins sum to it)
-    if (tid < 256) {
-      float c = 0.f;
-      for (int w = 0; w < kSampleWarps; ++w) c += hm[w * 256 + tid];
-      hc[tid] = __float_as_uint(c);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float z = 0.f;
-      for (int i = 0; i < 256; ++i) z += __uint_as_float(hc[i]);
-      s_f[0] = z;
-    }
-    __syncthreads();
-    const float target = top_p * s_f[0];
-    const uint32_t hb = pick_bin(true, target);
-    const float above = s_f[1];
+    fold_merge(true);
+    const uint32_t hb = pick_bin(true, 0.f, top_p);
+    const float target = s_f[0], above = s_f[1];
     __syncthreads();
     clear();
-    for_row([&](uint32_t k, float v, int64_t) {
-      if (k >= tk && (k >> 8) == hb) atomicAdd(&hm[warp * 256 + (k & 255u)], weight(v));
+    for_slice([&](uint32_t k, float v, int64_t) {
+      if (k >= tk && (k >> 8) == hb) atomicAdd(&hm[(k & 255u) * 32 + lane], weight(v));
     });
-    __syncthreads();
-    const uint32_t lb = pick_bin(true, target - above);
+    fold_merge(true);
+    const uint32_t lb = pick_bin(true, target - above, -1.f);
     const uint32_t tp = (hb << 8) | lb;
     t = tp > tk ? tp : tk;
   }
   // 4. inverse-CDF draw over kept tokens (key >= t), fixed visiting order
   float part = 0.f;
-  for_row([&](uint32_t k, float v, int64_t) { if (k >= t) part += weight(v); });
-  // inclusive block scan of the per-thread partial sums
+  for_slice([&](uint32_t k, float v, int64_t) { if (k >= t) part += weight(v); });
   float incl = part;
+#pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const float n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
+    const float nb = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += nb;
   }
   if (lane == 31) red[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    float w = lane < kSampleWarps ? red[lane] : 0.f;
+    float w = lane < kRowWarps ? red[lane] : 0.f;
+#pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float n = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += n;
+      const float nb = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += nb;
     }
-    if (lane < kSampleWarps) red[lane] = w;  // inclusive warp totals
+    if (lane < kRowWarps) red[lane] = w;  // inclusive warp totals
+    if (lane == kRowWarps - 1) mbuf[mb * 256] = w;  // this slice's kept mass
   }
-  __syncthreads();
-  const float before_warp = warp > 0 ? red[warp - 1] : 0.f;
-  const float total = red[kSampleWarps - 1];
-  const float excl = before_warp + incl - part;
+  cl_sync();
   const uint64_t r = splitmix64(seed ^ ((uint64_t)b * 0xD1B54A32D192ED03ull) ^
                                 ((uint64_t)(counters ? counters[b] : 0) << 32));
-  const float u = (float)(r >> 40) * (1.0f / 16777216.0f) * total;
-  __shared__ long long s_pick;
-  if (tid == 0) s_pick = -1;
-  __syncthreads();
+  if (tid == 0) {
+    // slice masses in rank order; the owner slice holds u (or, through
+    // rounding, the last slice with mass)
+    float sl[kRowCtas], total = 0.f;
+#pragma unroll
+    for (int q = 0; q < kRowCtas; ++q) { sl[q] = ld_peer_f32(mbuf + mb * 256, q); total += sl[q]; }
+    const float u = (float)(r >> 40) * (1.0f / 16777216.0f) * total;
+    int owner = -1, last = -1;
+    float before = 0.f, own_before = 0.f, last_before = 0.f;
+    for (int q = 0; q < kRowCtas; ++q) {
+      if (sl[q] > 0.f) {
+        last = q;
+        last_before = before;
+        if (owner < 0 && u >= before && u < before + sl[q]) { owner = q; own_before = before; }
+      }
+      before += sl[q];
+    }
+    if (owner < 0) { owner = last; own_before = last_before; }
+    s_owner = owner;
+    s_f[0] = u - own_before;  // u within the owner slice
+    s_pick = -1;
+  }
+  cl_sync();  // peers' shared memory is not read after this point
+  if ((int)cr != s_owner) {
+    if (s_owner < 0 && cr == 0 && tid == 0) out[b] = s_arg;
+    return;
+  }
+  const float u = s_f[0];
+  const float before_warp = warp > 0 ? red[warp - 1] : 0.f;
+  const float total = red[kRowWarps - 1];
+  const float excl = before_warp + incl - part;
   // the thread whose range holds u walks its elements again (same order and
   // arithmetic as `part`, so its running sum reproduces excl .. excl + part)
-  if (part > 0.f && u >= excl && (u < excl + part || tid == kSampleThreads - 1 ||
+  if (part > 0.f && u >= excl && (u < excl + part || tid == kRowThreads - 1 ||
                                    excl + part >= total)) {
     float run = excl;
-    int64_t last = -1, pick = -1;
-    for_row([&](uint32_t k, float v, int64_t i) {
+    long long lastk = -1, pick = -1;
+    for_slice([&](uint32_t k, float v, int64_t i) {
       if (k >= t && pick < 0) {
         run += weight(v);
-        last = i;
+        lastk = i;
         if (run > u) pick = i;
       }
     });
-    atomicMax(&s_pick, (long long)(pick >= 0 ? pick : last));
+    atomicMax(&s_pick, pick >= 0 ? pick : lastk);
   }
   __syncthreads();
   if (tid == 0) {
     // u fell between two threads' ranges through rounding: take the row max
-    const long long pk = s_pick >= 0 ? s_pick : s_arg;
-    out[b] = pk;
+    out[b] = s_pick >= 0 ? s_pick : s_arg;
   }
 }
 }  // namespace
@@ -434,13 +592,16 @@ extern "C" int tpp_sample(const void* logits, int64_t ld, int64_t B, int64_t V, 
   TPP_REQUIRE(aligned16(logits), TPP_ERR_ALIGN, "logits must be 16-byte aligned");
   TPP_REQUIRE(temperature > 0.f && top_p > 0.f && top_k >= 0, TPP_ERR_SHAPE,
               "need temperature > 0, top_p > 0, top_k >= 0 (greedy: tpp_argmax)");
-  const size_t smem = (size_t)kSampleWarps * 256 * 8 + kSampleWarps * 4;
+  const int64_t per = (V / 8 + kRowCtas - 1) / kRowCtas;
+  const size_t slice_bytes = (size_t)per * 16;
+  const bool staged = kSampleFixedSmem + slice_bytes <= 200 * 1024;
+  const size_t smem = kSampleFixedSmem + (staged ? slice_bytes : 0);
   const float itl = 1.4426950408889634f / temperature;
   return TPP_DISPATCH_HALF(dtype, T, [&] {
     cudaFuncSetAttribute(sample_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-    return launch("sample_kernel", sample_kernel<T>, dim3((unsigned)B), dim3(kSampleThreads),
-                  smem, as_stream(stream), 0u, (const T*)logits, ld, V, itl, top_k, top_p,
-                  seed, counters, out);
+    return launch("sample_kernel", sample_kernel<T>, dim3((unsigned)B, kRowCtas),
+                  dim3(kRowThreads), smem, as_stream(stream), (unsigned)kRowCtas,
+                  (const T*)logits, ld, V, itl, top_k, top_p, seed, counters, out, staged);
   });
 }
