@@ -305,6 +305,26 @@ def per_op(hbm_peak: float, tc_peak: float) -> dict:
         rec(f"cfg3_linear_silu_M{M_}_K1024_N3072_f16", t, nb, "GB/s")
         del Ws
 
+    # decode linears at batch 32 (bf16 activations), bf16 weights vs fp8
+    # weights (tpp_linear_fp8): LM head, gate/up (SwiGLU), qkv; several weight
+    # copies rotate so every launch streams from HBM.  Algorithmic bytes =
+    # weights + scales + x + y.
+    for rows_, K_, act_, name_ in ((151936, 1024, "none", "lm_head"),
+                                   (6144, 1024, "swiglu", "gate_up"),
+                                   (4096, 1024, "none", "qkv")):
+        n_out = rows_ // 2 if act_ == "swiglu" else rows_
+        io = 2 * 32 * (K_ + n_out)
+        xm = rnd(32, K_, dtype=torch.bfloat16)
+        n = copies(rows_ * K_)
+        Ws = [rnd(rows_, K_, std=0.02, dtype=torch.bfloat16) for _ in range(n)]
+        t = _time_graph([lambda i=i: ops.linear(xm, Ws[i], act=act_) for i in range(n)]) / n
+        rec(f"decode_{name_}_M32_bf16_weights", t, 2 * rows_ * K_ + io, "GB/s")
+        Fs = [ops.Fp8Weight(W, act_) for W in Ws]
+        del Ws
+        t = _time_graph([lambda i=i: ops.linear_fp8(xm, Fs[i]) for i in range(len(Fs))]) / len(Fs)
+        rec(f"decode_{name_}_M32_fp8_weights", t, rows_ * K_ + 4 * rows_ + io, "GB/s")
+        del Fs
+
     # on-device sampling of a decode step's logits (batch 32, Qwen3 vocabulary):
     # algorithmic bytes = one read of the logits
     lg = rnd(32, 151936, dtype=torch.bfloat16, std=3.0)

@@ -163,6 +163,30 @@ int tpp_linear_packed(const void* x_packed, const void* w_packed, const void* bi
                       const void* residual, void* y, int64_t ldy, void* y_packed, int64_t M,
                       int64_t N, int64_t K, float eps, int act, int dtype, void* stream);
 
+/* ---- fp8 (e4m3) decode weights -------------------------------------------
+ * Weight-only fp8 for the decode linears (the reference lists quantized
+ * GEMMs as future work, todo.md:24-29).  Format: per-row fp32 scale =
+ * amax(|w[n,:]|) / 448 (1 for a zero row); q[n,:] = e4m3(w / scale) with
+ * round-to-nearest-even and saturation.  Storage (tpp_fp8_weight_bytes):
+ * 32-row groups, [ceil(rows/32)][K/64][32 rows][64 B] (rows past `rows`
+ * zero), so a group is one contiguous block; inside each 64-wide k-block
+ * byte 16c + 4s + j of a row holds k = 16s + {2c, 2c+1, 2c+8, 2c+9}[j] (the
+ * MMA fragment order).  K must be a multiple of 64. */
+int64_t tpp_fp8_weight_bytes(int64_t rows, int64_t K);
+int tpp_quantize_weight_fp8(const void* w, int64_t rows, int64_t K, int dtype, void* q,
+                            float* scale, void* stream);
+/* w[n, k] = dtype(e4m3(q) * scale[n]) in natural k order. */
+int tpp_dequantize_weight_fp8(const void* q, const float* scale, int64_t rows, int64_t K,
+                              int dtype, void* w, void* stream);
+/* y = act(r * scale[n] * (x . q[n]) + bias) + residual for 1..32 tokens, as
+ * tpp_linear / tpp_rmsnorm_linear with the weight in the fp8 format above:
+ * r = rsqrt(mean(x^2) + eps) when eps >= 0 (norm weight folded into w
+ * before quantizing), else 1; SwiGLU: q and scale hold 2N rows, gate first
+ * (N a multiple of 8).  Larger M: tpp_dequantize_weight_fp8 + tpp_linear. */
+int tpp_linear_fp8(const void* x, int64_t ldx, const void* q, const float* scale,
+                   const void* bias, const void* residual, void* y, int64_t ldy, int64_t M,
+                   int64_t N, int64_t K, float eps, int act, int dtype, void* stream);
+
 /* One sampled token per row of logits [B, V] (row stride ld; V, ld multiples
  * of 8): softmax(logits / temperature) restricted to the top_k largest
  * logits (0 = no limit) and to the smallest descending prefix whose

@@ -153,3 +153,56 @@ def qk_norm_rope(x, w, eps, cos, sin, pos):
     c = f32(cos)[pos]
     s = f32(sin)[pos]
     return x * c + rotate_half(x) * s
+
+
+# ---- fp8 (e4m3) decode weights -------------------------------------------
+# The reference lists quantized GEMMs as future work (todo.md:24-29) and has
+# no implementation; the format is this build's: per-output-row scale =
+# amax / 448, bytes = e4m3(w / scale) (round to nearest even, saturated), and
+# inside each 64-wide k-block byte 16c + 4s + j holds k = 16s + {2c, 2c+1,
+# 2c+8, 2c+9}[j].  The tolerance of the fp8 linear is defined against the
+# dequantized weight (a weight-only format: activations stay bf16/fp16).
+
+def fp8_k_order(K):
+    """Logical k held by each stored byte position of a row (length K)."""
+    pos = torch.arange(64)
+    c, s, j = pos // 16, (pos // 4) % 4, pos % 4
+    blk = 16 * s + 2 * c + (j % 2) + (j // 2) * 8
+    return (torch.arange(0, K, 64)[:, None] + blk[None, :]).reshape(-1)
+
+
+def _group_rows(q):
+    """[rows, K] bytes (k already in stored order) -> the grouped storage
+    [ceil(rows/32)][K/64][32][64] as one flat uint8 tensor."""
+    rows, K = q.shape
+    G = (rows + 31) // 32
+    pad = torch.zeros(G * 32, K, dtype=torch.uint8)
+    pad[:rows] = q
+    return pad.view(G, 32, K // 64, 64).permute(0, 2, 1, 3).contiguous().view(-1)
+
+
+def _ungroup_rows(flat, rows, K):
+    G = (rows + 31) // 32
+    return flat.view(G, K // 64, 32, 64).permute(0, 2, 1, 3).reshape(G * 32, K)[:rows]
+
+
+def quantize_weight_fp8(w):
+    """w [rows, K] -> (flat uint8 storage, scale fp32 [rows]); the storage is
+    32-row groups [ceil(rows/32)][K/64][32][64 B], rows past `rows` zero."""
+    w = f32(w)
+    amax = w.abs().amax(dim=1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (w / scale[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    q = q[:, fp8_k_order(w.shape[1])].view(torch.uint8)
+    return _group_rows(q), scale
+
+
+def dequantize_weight_fp8(q, scale, K):
+    """Inverse of quantize_weight_fp8, fp32 [rows, K] in natural k order."""
+    q, scale = q.detach().cpu(), f32(scale)
+    rows = scale.shape[0]
+    vals = _ungroup_rows(q, rows, K).view(torch.float8_e4m3fn).to(torch.float32)
+    vals = vals * scale[:, None]
+    out = torch.empty_like(vals)
+    out[:, fp8_k_order(K)] = vals
+    return out

@@ -158,3 +158,26 @@ def test_engine_sampling_generate():
     assert int(a.max()) < 1000 and int(a.min()) >= 0
     assert torch.equal(a, b)
     assert not torch.equal(a, c)
+
+
+def test_engine_fp8_weights_track_native_engine():
+    """weight_format="fp8": the decode step on e4m3 weights gives logits within
+    the format's quantization error of the native step, from the same prefill."""
+    m = make(torch.bfloat16, seed=7)
+    ids = torch.randint(0, 1000, (3, 20), generator=torch.Generator().manual_seed(8))
+    with torch.inference_mode():
+        outs = []
+        for fmt in ("native", "fp8"):
+            eng = m.engine(3, 64, weight_format=fmt)
+            assert eng.weight_format == fmt
+            eng.prefill(ids)
+            eng.step_eager()
+            outs.append(eng.logits.float().clone())
+        # the greedy generate path runs through the fp8 engine as well
+        m.decode_weight_format = "fp8"
+        out = m.generate(ids, max_new_token=5, sampling_strategy="greedy")
+        m.decode_weight_format = "native"
+    ref, got = outs
+    rel = (got - ref).norm() / ref.norm()
+    assert rel.item() < 0.08, rel.item()
+    assert out.shape == (3, 25) and torch.equal(out[:, :20].cpu(), ids)

@@ -106,3 +106,42 @@ def test_gqa_golden_is_consistent_with_oracle_composition():
     o = O.attention(q, k, v, causal=True).reshape(B, S, 256)
     y = o @ sd["out_projection.weight"].T
     torch.testing.assert_close(y, G["gqa_y"], atol=2e-3, rtol=2e-3)
+
+
+# ---- fp8 weight format (oracle restatement) --------------------------------
+def test_fp8_k_order_is_a_permutation_of_each_block():
+    order = O.fp8_k_order(192)
+    assert sorted(order.tolist()) == list(range(192))
+    # byte 16c + 4s + j holds k = 16s + {2c, 2c+1, 2c+8, 2c+9}[j]
+    assert order[:8].tolist() == [0, 1, 8, 9, 16, 17, 24, 25]
+    assert order[16:20].tolist() == [2, 3, 10, 11]
+    assert order[64:68].tolist() == [64, 65, 72, 73]
+
+
+def test_fp8_rounding_known_answers():
+    # e4m3: 3 mantissa bits, max 448; ties round to even
+    w = torch.zeros(1, 64)
+    w[0, :8] = torch.tensor([448.0, 34.0, 38.0, -0.0625, 0.0, 1.0, -1.5, 100.0])
+    q, s = O.quantize_weight_fp8(w)
+    assert s.item() == 1.0
+    deq = O.dequantize_weight_fp8(q, s, 64)[0, :8]
+    assert deq.tolist() == [448.0, 32.0, 40.0, -0.0625, 0.0, 1.0, -1.5, 96.0]
+    # raw codes in the stored order (k = 0, 1 sit at bytes 0, 1)
+    assert q[0].item() == 0x7E and q[1].item() == 0x60
+    # one row pads to a 32-row group: 32 x 64 bytes, rows 1..31 zero
+    assert q.numel() == 32 * 64 and int(q[64:].sum()) == 0
+
+
+def test_fp8_round_trip_error_bound():
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(64, 1024, generator=g) * 0.02
+    w[3].zero_()
+    q, s = O.quantize_weight_fp8(w)
+    assert q.dtype == torch.uint8 and q.numel() == 64 * 1024
+    back = O.dequantize_weight_fp8(q, s, 1024)
+    assert torch.equal(back[3], torch.zeros(1024))
+    # relative spacing of e4m3 normals is 2^-3: error <= half an ulp of the
+    # value, or half the subnormal step 2^-10 * scale near zero
+    err = (back - w).abs()
+    bound = torch.maximum(w.abs() * 2.0 ** -4, s[:, None] * 2.0 ** -10)
+    assert (err <= bound * 1.0001).all()

@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_hgemv": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
     "tpp_l2_prefetch": (_i32, [_p, _i64, _p]),
     "tpp_sample": (_i32, [_p, _i64, _i64, _i64, _f32, _i64, _f32, C.c_uint64, _p, _p, _i32, _p]),
+    "tpp_fp8_weight_bytes": (_i64, [_i64, _i64]),
+    "tpp_quantize_weight_fp8": (_i32, [_p, _i64, _i64, _i32, _p, _p, _p]),
+    "tpp_dequantize_weight_fp8": (_i32, [_p, _p, _i64, _i64, _i32, _p, _p]),
+    "tpp_linear_fp8": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _i32,
+                              _i32, _p]),
     "tpp_packed_weight_bytes": (_i64, [_i64, _i64, _i32]),
     "tpp_packed_activation_bytes": (_i64, [_i64, _i64]),
     "tpp_pack_weight": (_i32, [_p, _i64, _i64, _i32, _i32, _p, _p]),

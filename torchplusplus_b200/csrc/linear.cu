@@ -19,6 +19,13 @@ int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
                    const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                    int act, int dtype, cudaStream_t st, float norm_eps, const void* wpk,
                    const void* xpk, void* ypk);
+int linear_xs_fp8(const void* x, int64_t ldx, const void* q, const float* scale,
+                  const void* bias, const void* residual, void* y, int64_t ldy, int64_t M,
+                  int64_t N, int64_t K, int act, int dtype, cudaStream_t st, float norm_eps);
+int quantize_weight_fp8(const void* w, int64_t rows, int64_t K, int dtype, void* q, float* scale,
+                        cudaStream_t st);
+int dequantize_weight_fp8(const void* q, const float* scale, int64_t rows, int64_t K, int dtype,
+                          void* w, cudaStream_t st);
 constexpr int64_t kDecodeMaxM = 64;
 }  // namespace tpp
 
@@ -113,4 +120,51 @@ extern "C" int tpp_linear_packed(const void* x_packed, const void* w_packed, con
               TPP_ERR_ALIGN, "a packed output needs N % 64 == 0 and 16-byte aligned rows");
   return linear_xs_impl(nullptr, K, nullptr, bias, residual, y, ldy, M, N, K, act, dtype,
                         as_stream(stream), eps, w_packed, x_packed, y_packed);
+}
+
+extern "C" int tpp_quantize_weight_fp8(const void* w, int64_t rows, int64_t K, int dtype, void* q,
+                                       float* scale, void* stream) {
+  if (rows == 0) return TPP_OK;
+  TPP_REQUIRE(w && q && scale, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(rows > 0 && rows <= 0x7fffffff && K > 0 && K <= 0x3fffffff && K % 64 == 0,
+              TPP_ERR_SHAPE, "need rows > 0 and K a positive multiple of 64");
+  TPP_REQUIRE(aligned16(w) && aligned16(q), TPP_ERR_ALIGN, "16-byte alignment required");
+  return quantize_weight_fp8(w, rows, K, dtype, q, scale, as_stream(stream));
+}
+
+extern "C" int64_t tpp_fp8_weight_bytes(int64_t rows, int64_t K) {
+  if (rows <= 0 || K <= 0 || K % 64 != 0 || rows > 0x7fffffff) return 0;
+  return (rows + 31) / 32 * 32 * K;
+}
+
+extern "C" int tpp_dequantize_weight_fp8(const void* q, const float* scale, int64_t rows,
+                                         int64_t K, int dtype, void* w, void* stream) {
+  if (rows == 0) return TPP_OK;
+  TPP_REQUIRE(w && q && scale, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(rows > 0 && K > 0 && K % 64 == 0 && rows * K < ((int64_t)1 << 46), TPP_ERR_SHAPE,
+              "need rows > 0 and K a positive multiple of 64");
+  return dequantize_weight_fp8(q, scale, rows, K, dtype, w, as_stream(stream));
+}
+
+extern "C" int tpp_linear_fp8(const void* x, int64_t ldx, const void* q, const float* scale,
+                              const void* bias, const void* residual, void* y, int64_t ldy,
+                              int64_t M, int64_t N, int64_t K, float eps, int act, int dtype,
+                              void* stream) {
+  if (M == 0) return TPP_OK;
+  TPP_REQUIRE(x && q && scale && y, TPP_ERR_SHAPE, "null pointer");
+  TPP_REQUIRE(M > 0 && M <= 32, TPP_ERR_UNSUPPORTED,
+              "fp8 decode linear serves 1..32 tokens (larger M: dequantize + tpp_linear)");
+  TPP_REQUIRE(N > 0 && N <= 0x3fffffff && K > 0 && K <= 0x3fffffff && K % 64 == 0,
+              TPP_ERR_SHAPE, "need N > 0 and K a positive multiple of 64");
+  TPP_REQUIRE(ldx >= K && ldy >= N, TPP_ERR_SHAPE, "row stride smaller than the row");
+  TPP_REQUIRE(act >= TPP_ACT_NONE && act <= TPP_ACT_SWIGLU, TPP_ERR_UNSUPPORTED, "unknown activation");
+  TPP_REQUIRE(ldx % 8 == 0 && aligned16(x) && aligned16(q), TPP_ERR_ALIGN,
+              "x rows and the fp8 weight must be 16-byte aligned");
+  const int rc = linear_xs_fp8(x, ldx, q, scale, bias, residual, y, ldy, M, N, K, act, dtype,
+                               as_stream(stream), eps);
+  if (rc == -1) {
+    set_error("tpp_linear_fp8: no launch plan for this shape");
+    return TPP_ERR_UNSUPPORTED;
+  }
+  return rc;
 }

@@ -238,6 +238,10 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int ab_bf16,
 template <typename T> struct IsBf16 { static constexpr int value = 0; };
 template <> struct IsBf16<__nv_bfloat16> { static constexpr int value = 1; };
 
+// Element type code of make_tmap for raw bytes (fp8 weights); beside the
+// public TPP_F16 / TPP_BF16 / TPP_F32 codes.
+constexpr int kTmapU8 = 100;
+
 // Host: builds a 2-D/3-D tiled tensor map through the driver entry point
 // (no link-time dependency on libcuda).  Returns TPP_OK or an error status.
 int make_tmap(CUtensorMap* map, const void* base, int dtype, int rank, const uint64_t* dims,

@@ -47,6 +47,7 @@ int make_tmap(CUtensorMap* map, const void* base, int dtype, int rank, const uin
     case TPP_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
     case TPP_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
     case TPP_F32: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    case kTmapU8: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
     default: set_error("make_tmap: bad dtype"); return TPP_ERR_DTYPE;
   }
   cuuint64_t d[5], s[4];

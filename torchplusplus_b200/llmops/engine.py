@@ -34,7 +34,8 @@ class DecodeEngine:
     graph (each weight is then read once per lane); the default is one lane
     (see the measurement noted below)."""
 
-    def __init__(self, model, batch_size: int, max_seq_len: int, lanes: int | None = None):
+    def __init__(self, model, batch_size: int, max_seq_len: int, lanes: int | None = None,
+                 weight_format: str = "native"):
         cfg = model.cfg
         dev = model.out_head.weight.device
         self.model = model
@@ -117,6 +118,22 @@ class DecodeEngine:
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step: int | None = None
         self.prompt_len = 0
+        # weight_format "fp8": the decode step's projections and LM head run
+        # on e4m3 copies of the (norm-folded) weights with per-row scales
+        # (tpp_linear_fp8, half the weight bytes); prefill keeps the model's
+        # own weights.  Lanes of up to 32 sequences.
+        if weight_format not in ("native", "fp8"):
+            raise ValueError("weight_format must be 'native' or 'fp8'")
+        self.weight_format = weight_format
+        self.lm_head_f8 = None
+        if weight_format == "fp8":
+            if max(ln["n"] for ln in self.lanes) > 32:
+                raise ValueError("fp8 decode weights serve lanes of at most 32 sequences")
+            for L in self.layers:
+                L["f8"] = dict(qkv=ops.Fp8Weight(L["wqkv_f"]), o=ops.Fp8Weight(L["wo"]),
+                               gu=ops.Fp8Weight(L["wgu_f"], "swiglu"),
+                               down=ops.Fp8Weight(L["wdown"]))
+            self.lm_head_f8 = ops.Fp8Weight(self.lm_head_f)
 
     # ------------------------------------------------------------ one step
     def _step_lane(self, ln: dict, warm: Optional[torch.cuda.Stream] = None) -> None:
@@ -124,7 +141,11 @@ class DecodeEngine:
         x = ln["x"]
         ops.embedding(ln["tokens"], self.emb, out=x)
         for L, kc, vc in zip(self.layers, ln["k"], ln["v"]):
-            ops.rmsnorm_linear(x, L["wqkv_f"], self.eps, out=ln["qkv"].view(n, -1))
+            f8 = L.get("f8")
+            if f8 is not None:
+                ops.linear_fp8(x, f8["qkv"], eps=self.eps, out=ln["qkv"].view(n, -1))
+            else:
+                ops.rmsnorm_linear(x, L["wqkv_f"], self.eps, out=ln["qkv"].view(n, -1))
             if warm is not None:
                 # parallel branch: pull this layer's remaining weights into L2
                 # while attention runs
@@ -145,10 +166,18 @@ class DecodeEngine:
                                        q_out=ln["q"])
                 ops.attention_decode(ln["q"].view(n, Hq, D), kc, vc, ln["seqlens"],
                                      self.max_seq_len, out=ln["o"], workspace=ln["ws"])
-            ops.linear(ln["o"].view(n, Hq * D), L["wo"], residual=x, out=x)
-            ops.rmsnorm_linear(x, L["wgu_f"], self.eps, act="swiglu", out=ln["ff"])
-            ops.linear(ln["ff"], L["wdown"], residual=x, out=x)
-        ops.rmsnorm_linear(x, self.lm_head_f, self.eps, out=ln["logits"])
+            if f8 is not None:
+                ops.linear_fp8(ln["o"].view(n, Hq * D), f8["o"], residual=x, out=x)
+                ops.linear_fp8(x, f8["gu"], eps=self.eps, out=ln["ff"])
+                ops.linear_fp8(ln["ff"], f8["down"], residual=x, out=x)
+            else:
+                ops.linear(ln["o"].view(n, Hq * D), L["wo"], residual=x, out=x)
+                ops.rmsnorm_linear(x, L["wgu_f"], self.eps, act="swiglu", out=ln["ff"])
+                ops.linear(ln["ff"], L["wdown"], residual=x, out=x)
+        if self.lm_head_f8 is not None:
+            ops.linear_fp8(x, self.lm_head_f8, eps=self.eps, out=ln["logits"])
+        else:
+            ops.rmsnorm_linear(x, self.lm_head_f, self.eps, out=ln["logits"])
         self._pick(ln["logits"], ln["positions"], ln["tokens"])
         ops.decode_advance(ln["tokens"], ln["out_ids"], ln["positions"], ln["seqlens"])
 

@@ -137,11 +137,16 @@ class Qwen3(LLMInference):
         x = self.final_rmsnorm(x)
         return ops.linear(x, self.out_head.weight)
 
-    def engine(self, batch_size: int, max_seq_len: int):
+    def engine(self, batch_size: int, max_seq_len: int, weight_format: str | None = None):
+        """The model's decode engine (rebuilt when the batch, capacity or
+        weight format changes).  weight_format: "native" or "fp8" (decode
+        projections on e4m3 weights); None keeps self.decode_weight_format."""
         from .engine import DecodeEngine
+        fmt = weight_format or getattr(self, "decode_weight_format", "native")
         e = self._engine
-        if e is None or e.batch_size != batch_size or e.max_seq_len < max_seq_len:
-            self._engine = e = DecodeEngine(self, batch_size, max_seq_len)
+        if e is None or e.batch_size != batch_size or e.max_seq_len < max_seq_len or \
+                e.weight_format != fmt:
+            self._engine = e = DecodeEngine(self, batch_size, max_seq_len, weight_format=fmt)
         return e
 
     @torch.inference_mode()

@@ -280,6 +280,69 @@ def linear_packed(x_packed: torch.Tensor, M: int, w: PackedWeight,
     return out
 
 
+class Fp8Weight:
+    """A linear weight quantized once to fp8 e4m3 with one fp32 scale per
+    output row (tpp_quantize_weight_fp8), in the decode kernel's k order.
+    `n` = outputs, `k` = inputs, `act` as for linear() (swiglu: [2N, K])."""
+
+    def __init__(self, weight: torch.Tensor, act: str = "none"):
+        _cuda(weight)
+        dt = _half(weight, "weight")
+        rows, K = weight.shape
+        if K % 64:
+            raise ValueError("fp8 weights need K a multiple of 64")
+        w = weight.contiguous()
+        # 32-row groups [ceil(rows/32)][K/64][32][64 B] (tpp_fp8_weight_bytes)
+        self.q = torch.empty(int(N.lib().tpp_fp8_weight_bytes(rows, K)), dtype=torch.uint8,
+                             device=weight.device)
+        self.scale = torch.empty(rows, dtype=torch.float32, device=weight.device)
+        N.call("tpp_quantize_weight_fp8", w.data_ptr(), rows, K, dt, self.q.data_ptr(),
+               self.scale.data_ptr(), N.stream_of(weight))
+        self.rows = rows
+        self.n = rows // 2 if act == "swiglu" else rows
+        self.k, self.act, self.dtype = K, act, weight.dtype
+
+    def dequantize(self) -> torch.Tensor:
+        """The weight this format represents, [rows, K] in self.dtype."""
+        out = torch.empty((self.rows, self.k), dtype=self.dtype, device=self.q.device)
+        N.call("tpp_dequantize_weight_fp8", self.q.data_ptr(), self.scale.data_ptr(),
+               self.rows, self.k, N.dtype_code(self.dtype), out.data_ptr(),
+               N.stream_of(self.q))
+        return out
+
+
+def linear_fp8(x: torch.Tensor, w: Fp8Weight, bias: torch.Tensor | None = None,
+               residual: torch.Tensor | None = None, eps: float | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = act(r * (x . W^T) + bias) + residual with W the fp8 weight;
+    r = rsqrt(mean(x^2) + eps) when eps is given (norm weight folded into W
+    before quantizing).  Up to 32 tokens run the fp8 decode kernel; more go
+    through the dequantized weight and the GEMM path."""
+    _cuda(x, bias, residual, out)
+    dt = _half(x, "x")
+    if x.dtype != w.dtype:
+        raise TypeError("x and the fp8 weight's compute dtype differ")
+    K = w.k
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if M > 32:
+        wd = w.dequantize()
+        if eps is not None:
+            ones = torch.ones(K, dtype=x.dtype, device=x.device)
+            x = rmsnorm(x, ones, eps)
+        return linear(x, wd, bias, w.act, residual, out)
+    if x2.stride(-1) != 1 or (M > 1 and x2.stride(0) % 8):
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty((*x.shape[:-1], w.n), dtype=x.dtype, device=x.device)
+    y2 = out.view(-1, w.n)
+    r2 = residual.contiguous().view(-1, w.n) if residual is not None else None
+    N.call("tpp_linear_fp8", x2.data_ptr(), x2.stride(0) if M > 1 else K, w.q.data_ptr(),
+           w.scale.data_ptr(), N.ptr(bias), N.ptr(r2), y2.data_ptr(), w.n, M, w.n, K,
+           -1.0 if eps is None else float(eps), N.ACT_CODE[w.act], dt, N.stream_of(x))
+    return out
+
+
 def l2_prefetch(t: torch.Tensor) -> None:
     """Bulk-prefetch a (contiguous) tensor's bytes into L2 on the current stream."""
     _cuda(t)
