@@ -450,6 +450,7 @@ def run_ours(args, rank, world, local):
         e1.prefill(prompts[0][:1])
         e1.capture()
         e1.decode(8)
+        e1.prefill(prompts[0][:1])  # back to the prompt: nrep steps fill the capacity
         torch.cuda.synchronize()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
@@ -458,6 +459,27 @@ def run_ours(args, rank, world, local):
         a1.synchronize()
         extra["batch1_decode_tokens_per_s"] = nrep / (a0.elapsed_time(a1) / 1e3)
         model._engine = None
+    if rank == 0 and not args.skip_fp8:
+        # the same decode with fp8 (e4m3, per-row scale) copies of the
+        # projection and LM-head weights (weight_format="fp8") or of the LM
+        # head alone ("fp8_head"); reported beside, not as, the headline (the
+        # reference's weights are bf16)
+        for fmt, bsz in (("fp8", B), ("fp8", 1), ("fp8_head", B), ("fp8_head", 1)):
+            ef = model.engine(bsz, cap, weight_format=fmt)
+            ef.prefill(prompts[0][:bsz])
+            ef.capture()
+            ef.decode(8)
+            ef.prefill(prompts[0][:bsz])
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            ef.decode(nrep)
+            a1.record()
+            a1.synchronize()
+            extra[f"{fmt}_weights_batch{bsz}_decode_tokens_per_s"] = \
+                bsz * nrep / (a0.elapsed_time(a1) / 1e3)
+            model._engine = None
+            del ef
 
     lps = eng.launches_per_step or 0
     ops_res = None
@@ -502,6 +524,7 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-b1", action="store_true")
     ap.add_argument("--skip-ops", action="store_true", help="skip the per-op roofline table")
+    ap.add_argument("--skip-fp8", action="store_true", help="skip the fp8-weights decode lines")
     ap.add_argument("--gen", type=int, default=GEN,
                     help="tokens generated per request (profiling runs use fewer)")
     args = ap.parse_args()

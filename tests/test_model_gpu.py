@@ -167,7 +167,7 @@ def test_engine_fp8_weights_track_native_engine():
     ids = torch.randint(0, 1000, (3, 20), generator=torch.Generator().manual_seed(8))
     with torch.inference_mode():
         outs = []
-        for fmt in ("native", "fp8"):
+        for fmt in ("native", "fp8", "fp8_head"):
             eng = m.engine(3, 64, weight_format=fmt)
             assert eng.weight_format == fmt
             eng.prefill(ids)
@@ -177,7 +177,26 @@ def test_engine_fp8_weights_track_native_engine():
         m.decode_weight_format = "fp8"
         out = m.generate(ids, max_new_token=5, sampling_strategy="greedy")
         m.decode_weight_format = "native"
-    ref, got = outs
-    rel = (got - ref).norm() / ref.norm()
-    assert rel.item() < 0.08, rel.item()
+    ref = outs[0]
+    for got in outs[1:]:
+        rel = (got - ref).norm() / ref.norm()
+        assert rel.item() < 0.08, rel.item()
     assert out.shape == (3, 25) and torch.equal(out[:, :20].cpu(), ids)
+
+
+def test_engine_refuses_steps_beyond_capacity():
+    """Decode steps write K/V rows and output ids past the prompt without a
+    device-side bound check, so the host refuses steps past the capacity."""
+    m = make(torch.bfloat16, seed=9)
+    ids = torch.randint(0, 1000, (2, 20), generator=torch.Generator().manual_seed(10))
+    with torch.inference_mode():
+        eng = m.engine(2, 32)
+        eng.prefill(ids)
+        eng.decode(11)                 # positions 20..30, last id at 31: fits
+        with pytest.raises(ValueError):
+            eng.decode(1)
+        with pytest.raises(ValueError):
+            eng.step_eager()
+        eng.prefill(ids)               # prefill resets the position
+        eng.decode(3)
+    assert eng.out_ids.shape == (2, 32)

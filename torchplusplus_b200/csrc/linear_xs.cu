@@ -146,6 +146,19 @@ __device__ __forceinline__ uint32_t e4m3x2_to(uint32_t v16) {
   }
 }
 
+// Global loads issued where they are written (asm volatile keeps them ahead
+// of the MMA loop instead of being sunk next to their use).
+__device__ __forceinline__ float ldg_early_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ldg_early_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -569,14 +582,14 @@ __global__ void __launch_bounds__(xs_threads(NTM), NTM > 4 ? 1 : (BN == 16 ? 3 :
 //    prescale (largest |x| below 2^14: exact, no overflow), so each pair of
 //    e4m3 weights becomes an MMA operand with one cvt.rn.f16x2.e4m3x2; the
 //    epilogue undoes the prescale.
-//  * The eight compute warps form two teams of four that take alternate
+//  * The twelve compute warps form three teams of four that take turns on
 //    groups (the CTA's groups blockIdx.x, blockIdx.x + gridDim.x, ...): warp
 //    w of a team multiplies k-blocks w, w + 4, ...; the team's partial sums
 //    meet in its own shared-memory buffer; the epilogue (per-row scale,
 //    norm factor, bias, activation, residual; scales and bias loaded when
-//    the group starts) runs while the other team multiplies.
+//    the group starts) runs while the other teams multiply.
 // ---------------------------------------------------------------------------
-constexpr int kWideKW = 8;       // compute warps (two teams of four)
+constexpr int kWideKW = 12;      // compute warps (three teams of four)
 constexpr int kWideTW = 4;       // warps per team
 constexpr int kWideNR = 32;      // weight rows per group
 constexpr int kWideStages = 3;   // weight ring depth
@@ -692,8 +705,9 @@ __global__ void __launch_bounds__((kWideKW + 1) * 32, 1)
     if (lane == 0)
       tokf[t] = ldexpf(1.f, -ex) * (NORM ? rsqrtf(ss / (float)p.K + p.eps) : 1.f);
   }
-  asm volatile("bar.sync 3, %0;" ::"n"(KW * 32) : "memory");
+  asm volatile("bar.sync 8, %0;" ::"n"(KW * 32) : "memory");
 
+  constexpr int TEAMS = KW / TW;
   const int team = warp / TW, wt = warp % TW, ttid = threadIdx.x % (TW * 32);
   uint32_t offa[4][MT];
 #pragma unroll
@@ -716,15 +730,20 @@ __global__ void __launch_bounds__((kWideKW + 1) * 32, 1)
   const float etf = has_item ? tokf[et] : 0.f;
 
   int it = team;
-  for (int g = blockIdx.x + team * gridDim.x; g < groups; g += 2 * gridDim.x, it += 2) {
+  for (int g = blockIdx.x + team * gridDim.x; g < groups; g += TEAMS * gridDim.x, it += TEAMS) {
     const int s = it % S;
     const int n0 = g * kWideNR + ec0;
     float sc[8], bs[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const bool in = has_item && n0 + i < p.N;
-      sc[i] = in ? __ldg(p.wscale + n0 + i) : 0.f;
-      bs[i] = in && bias ? to_f32(bias[n0 + i]) : 0.f;
+      sc[i] = in ? ldg_early_f32(p.wscale + n0 + i) : 0.f;
+      if (in && bias) {
+        const uint16_t h = ldg_early_u16(bias + n0 + i);
+        bs[i] = to_f32(*reinterpret_cast<const T*>(&h));
+      } else {
+        bs[i] = 0.f;
+      }
     }
     float acc[MT][NT][4];
 #pragma unroll
@@ -760,8 +779,7 @@ __global__ void __launch_bounds__((kWideKW + 1) * 32, 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
     // the team's previous epilogue has finished reading its partials
-    if (team == 0) asm volatile("bar.sync 1, %0;" ::"n"(TW * 32) : "memory");
-    else asm volatile("bar.sync 2, %0;" ::"n"(TW * 32) : "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "n"(TW * 32) : "memory");
     {
       const int gq = lane >> 2, cq = lane & 3;
 #pragma unroll
@@ -773,8 +791,7 @@ __global__ void __launch_bounds__((kWideKW + 1) * 32, 1)
           *reinterpret_cast<float2*>(r0 + 8 * RST) = make_float2(acc[mi][ni][2], acc[mi][ni][3]);
         }
     }
-    if (team == 0) asm volatile("bar.sync 1, %0;" ::"n"(TW * 32) : "memory");
-    else asm volatile("bar.sync 2, %0;" ::"n"(TW * 32) : "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "n"(TW * 32) : "memory");
     if (!ok || !has_item || n0 >= p.N) continue;
     float o[8];
 #pragma unroll

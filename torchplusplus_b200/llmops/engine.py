@@ -118,22 +118,27 @@ class DecodeEngine:
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step: int | None = None
         self.prompt_len = 0
+        self._pos = 0  # host copy of the next write position (all sequences)
         # weight_format "fp8": the decode step's projections and LM head run
         # on e4m3 copies of the (norm-folded) weights with per-row scales
-        # (tpp_linear_fp8, half the weight bytes); prefill keeps the model's
-        # own weights.  Lanes of up to 32 sequences.
-        if weight_format not in ("native", "fp8"):
-            raise ValueError("weight_format must be 'native' or 'fp8'")
+        # (tpp_linear_fp8, half the weight bytes); "fp8_head": only the LM
+        # head (the one decode linear that is bandwidth-bound, so the only one
+        # fp8 makes faster on B200; the per-layer projections are latency-
+        # bound).  Prefill keeps the model's own weights.  Lanes of up to 32
+        # sequences.
+        if weight_format not in ("native", "fp8", "fp8_head"):
+            raise ValueError("weight_format must be 'native', 'fp8' or 'fp8_head'")
         self.weight_format = weight_format
         self.lm_head_f8 = None
-        if weight_format == "fp8":
+        if weight_format != "native":
             if max(ln["n"] for ln in self.lanes) > 32:
                 raise ValueError("fp8 decode weights serve lanes of at most 32 sequences")
+            self.lm_head_f8 = ops.Fp8Weight(self.lm_head_f)
+        if weight_format == "fp8":
             for L in self.layers:
                 L["f8"] = dict(qkv=ops.Fp8Weight(L["wqkv_f"]), o=ops.Fp8Weight(L["wo"]),
                                gu=ops.Fp8Weight(L["wgu_f"], "swiglu"),
                                down=ops.Fp8Weight(L["wdown"]))
-            self.lm_head_f8 = ops.Fp8Weight(self.lm_head_f)
 
     # ------------------------------------------------------------ one step
     def _step_lane(self, ln: dict, warm: Optional[torch.cuda.Stream] = None) -> None:
@@ -208,6 +213,7 @@ class DecodeEngine:
 
     def step_eager(self) -> None:
         """One decode step launched directly (no graph); used by tests."""
+        self._advance(1)
         self._step()
 
     def capture(self) -> None:
@@ -264,8 +270,18 @@ class DecodeEngine:
         self.positions.fill_(S)
         self.seqlens.fill_(S + 1)
         self.prompt_len = S
+        self._pos = S
+
+    def _advance(self, steps: int) -> None:
+        # every step writes one K/V row at the current position and the next
+        # output id after it; the device does not bound-check those writes
+        if self._pos + steps > self.max_seq_len - 1:
+            raise ValueError(f"{steps} more decode steps from position {self._pos} exceed the "
+                             f"engine's capacity of {self.max_seq_len} (prefill again first)")
+        self._pos += steps
 
     def decode(self, steps: int) -> None:
+        self._advance(steps)
         if self.graph is None or self._graph_sampling != self.sampling:
             self.capture()
         for _ in range(steps):
