@@ -368,22 +368,38 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
     if (i < 10) DEC_TS(3 + i);
     const uint32_t vb = smem_u32(ring + s * 2 * SM::kTile) + SM::kTile;
     const int64_t kbase = k0 + (int64_t)i * KT + kr0;
+    if (kbase >= lo && kbase + 16 <= k1) {  // this warp's 16 keys all in range
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int64_t key = kbase + j * 8 + 2 * c + (e & 1);
-        sc[j][e] = (key < k1 && key >= lo) ? sc[j][e] * p.scale_log2 : -INFINITY;
-      }
+        for (int e = 0; e < 4; ++e) sc[j][e] *= p.scale_log2;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t key = kbase + j * 8 + 2 * c + (e & 1);
+          sc[j][e] = (key < k1 && key >= lo) ? sc[j][e] * p.scale_log2 : -INFINITY;
+        }
+    }
+    // Lazy rescale: the exponent base m_r moves (and o, l are rescaled) only
+    // when a row's maximum grows by more than 2^8 (log2 units); otherwise the
+    // probabilities are taken against the old base (at most 2^8 in fp32).
     float corr[2];
+    bool grow = false;
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
-      float mx = fmaxf(m_r[hr], fmaxf(fmaxf(sc[0][2 * hr], sc[0][2 * hr + 1]),
-                                      fmaxf(sc[1][2 * hr], sc[1][2 * hr + 1])));
+      float mx = fmaxf(fmaxf(sc[0][2 * hr], sc[0][2 * hr + 1]),
+                       fmaxf(sc[1][2 * hr], sc[1][2 * hr + 1]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      corr[hr] = (mx == -INFINITY) ? 1.f : exp2f(m_r[hr] - mx);
-      m_r[hr] = mx;
+      corr[hr] = 1.f;
+      if (mx > m_r[hr] + 8.f) {
+        corr[hr] = exp2f(m_r[hr] - mx);  // 0 when no key was seen yet
+        m_r[hr] = mx;
+        grow = true;
+      }
+      mx = m_r[hr];
       float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
@@ -396,10 +412,12 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
         }
       l_r[hr] = l_r[hr] * corr[hr] + sum;
     }
+    if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-    for (int d = 0; d < D / 8; ++d) {
-      o[d][0] *= corr[0]; o[d][1] *= corr[0];
-      o[d][2] *= corr[1]; o[d][3] *= corr[1];
+      for (int d = 0; d < D / 8; ++d) {
+        o[d][0] *= corr[0]; o[d][1] *= corr[0];
+        o[d][2] *= corr[1]; o[d][3] *= corr[1];
+      }
     }
     uint32_t pa[4];
     pa[0] = pack2<T>(sc[0][0], sc[0][1]);
