@@ -313,11 +313,9 @@ __global__ void __launch_bounds__(xs_threads(NTM), NTM > 4 ? 1 : (BN == 16 ? 3 :
       }
     const uint32_t offw = (uint32_t)((lane >> 2) * 64 + (lane & 3) * 16);
     // stage layout [half][k-block][NRO rows][64 B] (half: SwiGLU gate / up)
-    constexpr int HN = SWIGLU ? NTM / 2 : NTM;      // n-tiles per half (register tile)
     const int hn = SWIGLU ? NT / 2 : NT;            // n-tiles per half
     const uint32_t xstride = BN * 128, wstride = (uint32_t)NRO * 64;
     const uint32_t hstride = (uint32_t)KC * NRO * 64;
-    (void)HN;
     for (int c = 0; c < NCH && ok; ++c) {
       const int s = c % S;
       ok = mbar_wait(&full[s], (c / S) & 1, p.err, 22);
