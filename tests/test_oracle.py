@@ -145,3 +145,18 @@ def test_fp8_round_trip_error_bound():
     err = (back - w).abs()
     bound = torch.maximum(w.abs() * 2.0 ** -4, s[:, None] * 2.0 ** -10)
     assert (err <= bound * 1.0001).all()
+
+
+def test_fp8_grouped_storage_round_trip_ragged_rows():
+    # 37 rows: two 32-row groups, the second padded with 27 zero rows
+    g = torch.Generator().manual_seed(6)
+    w = torch.randn(37, 128, generator=g)
+    q, s = O.quantize_weight_fp8(w)
+    assert q.numel() == 64 * 128
+    # group 1, k-block 0 holds rows 32..63; rows 37..63 are zero
+    blk = q.view(2, 2, 32, 64)
+    assert int(blk[1, :, 5:].abs().sum()) == 0
+    back = O.dequantize_weight_fp8(q, s, 128)
+    assert back.shape == (37, 128)
+    assert ((back - w).abs() <= torch.maximum(w.abs() * 2.0 ** -4, s[:, None] * 2.0 ** -10)
+            * 1.0001).all()
