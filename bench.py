@@ -1,6 +1,6 @@
 """Benchmark: Qwen3-0.6B-shaped greedy decode (bf16) on B200.
 
-Workload (batch 32 per GPU): random-init weights
+Workload (the Qwen3-0.6B-shaped decode configuration, batch 32 per GPU): random-init weights
 ~N(0, 0.02) of the Qwen3-0.6B shape, a prompt of 512 random token ids per
 sequence, then 256 greedy decode steps with the KV cache.  One bench step =
 one such request batch: prefill (untimed for `value`) + 255 decode steps
@@ -42,10 +42,22 @@ METRIC = "decode tokens/sec (Qwen3-0.6B shape) at 1/2/4/8 B200; per-op % of HBM/
 PROMPT, GEN = 512, 256
 
 
-# DRAM bytes (read + write) per decode-linear launch, measured by ncu on this
-# bench's own command (profiles/decode_linears_dram_qwen3_b32.md): 10.787 MB
-# against 10.93 MB algorithmic -- the weights are read once.
-LINEAR_DRAM_BYTES_PER_LAUNCH = 10.787e6
+# Measured DRAM traffic of the decode linears (ncu dram__bytes_read.sum +
+# dram__bytes_write.sum on `bench.py --one-op decode_linears`), kept as one
+# machine-readable line in the committed kernel summary; None when absent.
+TRAFFIC_SUMMARY = ROOT / "profiles" / "decode_linears_traffic_qwen3_b32.md"
+
+
+def linear_traffic_per_launch() -> float | None:
+    """Mean DRAM bytes per launch over one decode step's linear launches
+    (4 per layer x 28 + LM head), from the summary's `traffic_bytes_per_launch:`."""
+    try:
+        for line in TRAFFIC_SUMMARY.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
 
 
 def peaks():
@@ -233,7 +245,8 @@ def _time_graph(fn_list, reps: int = 5) -> float:
 
 
 def per_op(hbm_peak: float, tc_peak: float) -> dict:
-    """Per-op achieved throughput on the BASELINE configs 1, 2, 3 and 5.
+    """Per-op achieved throughput on the op-level configurations (1: RMSNorm +
+    Linear+SiLU, 2: RoPE + causal GQA prefill, 3: decode GEMVs, 5: SWA decode).
 
     Each op is launched over enough distinct input copies that the bytes
     touched per replay exceed L2 (126 MB), so every launch streams from HBM;
@@ -368,6 +381,121 @@ def per_op(hbm_peak: float, tc_peak: float) -> dict:
     return res
 
 
+ONE_OPS = ("rmsnorm", "linear_silu", "qkrope", "attention_prefill", "prefill_attn_d64",
+           "hgemv_lm_head", "hgemv_k1024_n3072", "decode_linears", "decode_attention",
+           "qk_norm_rope_cache", "swa_decode", "argmax", "sample", "embedding", "lm_head_fp8")
+
+
+def one_op(name: str, reps: int) -> dict:
+    """Builds one op's operands at its benchmark shape and launches it `reps`
+    times (no graph, synchronised): the small, self-contained command the
+    per-kernel ncu captures run on (a few GB on the device at most)."""
+    from torchplusplus_b200 import ops
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, dtype=torch.float16, std=1.0, mean=0.0):
+        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std
+                + mean).to(dtype)
+    bf = torch.bfloat16
+    fn = None
+    if name == "rmsnorm":                      # config 1
+        x, w = rnd(2048, 1024), rnd(1024, mean=1.0, std=0.1)
+        y = torch.empty_like(x)
+        fn = lambda: ops.rmsnorm(x, w, 1e-6, out=y)  # noqa: E731
+    elif name == "linear_silu":                # config 1
+        x, W = rnd(2048, 1024), rnd(3072, 1024, std=0.02)
+        y = torch.empty(2048, 3072, device=dev, dtype=torch.float16)
+        fn = lambda: ops.linear(x, W, act="silu", out=y)  # noqa: E731
+    elif name == "qkrope":                     # config 2
+        q, k = rnd(4, 16, 2048, 128), rnd(4, 8, 2048, 128)
+        cos, sin = rnd(2048, 128), rnd(2048, 128)
+        fn = lambda: ops.qkrope(q, k, cos, sin)  # noqa: E731
+    elif name == "attention_prefill":          # config 2 (tcgen05 kernel, D 128)
+        q, k, v = rnd(4, 2048, 16, 128), rnd(4, 2048, 8, 128), rnd(4, 2048, 8, 128)
+        o = torch.empty_like(q)
+        fn = lambda: ops.attention(q, k, v, causal=True, out=o)  # noqa: E731
+    elif name == "prefill_attn_d64":           # register-tile kernel (head dim 64)
+        q, k, v = rnd(4, 2048, 16, 64), rnd(4, 2048, 8, 64), rnd(4, 2048, 8, 64)
+        o = torch.empty_like(q)
+        fn = lambda: ops.attention(q, k, v, causal=True, out=o)  # noqa: E731
+    elif name == "hgemv_lm_head":              # config 3, K 1024 N 151936
+        W, x = rnd(151936, 1024, std=0.02), rnd(1024)
+        fn = lambda: ops.hgemv(W, x)  # noqa: E731
+    elif name == "hgemv_k1024_n3072":          # config 3
+        W, x = rnd(3072, 1024, std=0.02), rnd(1024)
+        fn = lambda: ops.hgemv(W, x)  # noqa: E731
+    elif name == "decode_linears":   # one Qwen3 layer's projections + LM head, 32 tokens
+        x, o, ff = rnd(32, 1024, dtype=bf), rnd(32, 2048, dtype=bf), rnd(32, 3072, dtype=bf)
+        wqkv, wo = rnd(4096, 1024, std=0.02, dtype=bf), rnd(1024, 2048, std=0.02, dtype=bf)
+        wgu, wd = rnd(6144, 1024, std=0.02, dtype=bf), rnd(1024, 3072, std=0.02, dtype=bf)
+        wh = rnd(151936, 1024, std=0.02, dtype=bf)
+        qkv, r = torch.empty(32, 4096, device=dev, dtype=bf), x.clone()
+        lg = torch.empty(32, 151936, device=dev, dtype=bf)
+
+        def fn():
+            ops.rmsnorm_linear(x, wqkv, 1e-6, out=qkv)
+            ops.linear(o, wo, residual=r, out=r)
+            ops.rmsnorm_linear(x, wgu, 1e-6, act="swiglu", out=ff)
+            ops.linear(ff, wd, residual=r, out=r)
+            ops.rmsnorm_linear(x, wh, 1e-6, out=lg)
+    elif name in ("decode_attention", "qk_norm_rope_cache"):   # Qwen3 layer, 32 tokens
+        B, Hq, Hkv, D, cap, pos = 32, 16, 8, 128, 768, 640
+        qkv = rnd(B, 1, (Hq + 2 * Hkv) * D, dtype=bf)
+        qn, kn = rnd(D, mean=1.0, std=0.1, dtype=bf), rnd(D, mean=1.0, std=0.1, dtype=bf)
+        from torchplusplus_b200.dlops.rope import compute_rope_params
+        cos, sin = compute_rope_params(D, 1e6, cap, device=dev)
+        kc, vc = rnd(B, Hkv, cap, D, dtype=bf), rnd(B, Hkv, cap, D, dtype=bf)
+        p = torch.full((B,), pos, dtype=torch.int32, device=dev)
+        sl = p + 1
+        o = torch.empty(B, Hq, D, device=dev, dtype=bf)
+        ws = torch.empty(max(16, ops.decode_workspace_bytes(B, Hq, cap, D)), dtype=torch.uint8,
+                         device=dev)
+        if name == "decode_attention":
+            fn = lambda: ops.attention_decode_qkv(  # noqa: E731
+                qkv, qn, kn, 1e-6, cos, sin, p, kc, vc, sl, cap, Hq, Hkv, out=o, workspace=ws)
+        else:
+            q = torch.empty(B, 1, Hq, D, device=dev, dtype=bf)
+            fn = lambda: ops.qk_norm_rope_cache(qkv, qn, kn, 1e-6, cos, sin, p, kc,  # noqa: E731
+                                                vc, Hq, Hkv, q_out=q)
+    elif name == "swa_decode":                 # config 5 at L 4096 (1 GB of cache)
+        B, L = 64, 4096
+        kc, vc = rnd(B, 8, L, 128, dtype=bf), rnd(B, 8, L, 128, dtype=bf)
+        q = rnd(B, 16, 128, dtype=bf)
+        o = torch.empty_like(q)
+        sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+        fn = lambda: ops.attention_decode(q, kc, vc, sl, L, window_left=4095, out=o)  # noqa: E731
+    elif name in ("argmax", "sample"):         # decode step's logits, 32 x 151936
+        lg = rnd(32, 151936, dtype=bf, std=3.0)
+        cnt = torch.arange(32, dtype=torch.int32, device=dev)
+        tok = torch.empty(32, dtype=torch.int64, device=dev)
+        if name == "argmax":
+            fn = lambda: ops.argmax(lg, out=tok)  # noqa: E731
+        else:
+            fn = lambda: ops.sample(lg, 0.8, 0, 0.9, 1, counters=cnt, out=tok)  # noqa: E731
+    elif name == "embedding":                  # 32 token rows of the Qwen3 table
+        tab = rnd(151936, 1024, dtype=bf, std=0.02)
+        ids = torch.randint(0, 151936, (32,), device=dev)
+        y = torch.empty(32, 1024, device=dev, dtype=bf)
+        fn = lambda: ops.embedding(ids, tab, out=y)  # noqa: E731
+    elif name == "lm_head_fp8":                # fp8 LM head, 32 tokens
+        W = ops.Fp8Weight(rnd(151936, 1024, std=0.02, dtype=bf))
+        x = rnd(32, 1024, dtype=bf)
+        y = torch.empty(32, 151936, device=dev, dtype=bf)
+        fn = lambda: ops.linear_fp8(x, W, eps=1e-6, out=y)  # noqa: E731
+    else:
+        raise SystemExit(f"--one-op: unknown op {name!r}; one of {', '.join(ONE_OPS)}")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    return {"one_op": name, "reps": reps, "us_per_rep": e0.elapsed_time(e1) * 1e3 / reps}
+
+
 def run_ours(args, rank, world, local):
     from torchplusplus_b200 import _native as N
     from torchplusplus_b200.llmops.qwen3 import Qwen3, Qwen3Config
@@ -437,10 +565,10 @@ def run_ours(args, rank, world, local):
                           "linear_skinny_kernel (LM head), 113 launches per step",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind}",
-                "traffic": LINEAR_DRAM_BYTES_PER_LAUNCH,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over one "
-                                  "decode step's 113 linear launches "
-                                  "(profiles/decode_linears_dram_qwen3_b32.md)",
+                "traffic": linear_traffic_per_launch(),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same "
+                                  "kernels at the same shapes (--one-op decode_linears), "
+                                  "weighted to one step's 113 launches",
                 "bytes_per_launch": rl["bytes_per_launch"],
                 "avg_launch_us": rl["avg_launch_s"] * 1e6,
                 "step_linear_time_us": rl["seconds"] * 1e6}
@@ -527,8 +655,17 @@ def main():
     ap.add_argument("--skip-fp8", action="store_true", help="skip the fp8-weights decode lines")
     ap.add_argument("--gen", type=int, default=GEN,
                     help="tokens generated per request (profiling runs use fewer)")
+    ap.add_argument("--one-op", default=None, choices=ONE_OPS,
+                    help="launch one op at its benchmark shape --reps times and exit "
+                         "(the command per-kernel ncu captures run on)")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
     GEN = args.gen
+    if args.one_op:
+        torch.cuda.set_device(0)
+        with torch.inference_mode():
+            print(json.dumps(one_op(args.one_op, args.reps)), flush=True)
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", 0))
         run_reference(args, rank, int(os.environ.get("WORLD_SIZE", 1)))

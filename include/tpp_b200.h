@@ -63,6 +63,11 @@ uint64_t tpp_launch_count(void);
  * the flag could not be read.  No reference counterpart (the reference has
  * no device-side waits). */
 int tpp_device_error(void* stream);
+/* Test hook for the path above: launches one CTA whose mbarrier wait can
+ * never complete (nothing arrives, no copy is in flight) with a limit of
+ * `polls` (1..65536) try_wait polls; the wait gives up, sets the flag to
+ * `code` (nonzero) and the kernel returns.  No reference counterpart. */
+int tpp_debug_expire_wait(uint32_t polls, int code, void* stream);
 
 /* ---- normalisation -------------------------------------------------------- */
 /* y[r,:] = x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w     (fp32 statistics)
@@ -231,6 +236,13 @@ int tpp_attention_prefill(const void* q, int64_t q_sb, int64_t q_ss, int64_t q_s
 /* Bytes of workspace tpp_attention_decode needs for the given shape. */
 int64_t tpp_attention_decode_workspace(int64_t B, int64_t Hq, int64_t max_seqlen,
                                        int64_t D);
+
+/* Exact workspace bytes for one decode-attention shape (this Hkv and window);
+ * 0 when the key range is merged without a workspace.  Never more than
+ * tpp_attention_decode_workspace(B, Hq, max_seqlen, D). */
+int64_t tpp_attention_decode_workspace_exact(int64_t B, int64_t Hq, int64_t Hkv,
+                                             int64_t max_seqlen, int64_t D,
+                                             int64_t window_left);
 
 /* Decode attention: one query token per sequence against the KV cache.
  *   q [B,Hq,D] (strides q_sb, q_sh); caches [B,Hkv,Smax,D] (strides c_sb,

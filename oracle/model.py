@@ -14,8 +14,9 @@ from . import ops as O
 
 
 @torch.no_grad()
-def forward(sd: dict, cfg, ids: torch.Tensor) -> torch.Tensor:
-    """ids [B, S] -> logits [B, S, V] (fp32), full causal attention, no cache."""
+def forward(sd: dict, cfg, ids: torch.Tensor, last_only: bool = False) -> torch.Tensor:
+    """ids [B, S] -> logits [B, S, V] (fp32), full causal attention, no cache;
+    last_only: the LM head on the last position only -> [B, 1, V]."""
     f = {k: v.detach().float().cpu() for k, v in sd.items()}
     B, S = ids.shape
     Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -36,6 +37,8 @@ def forward(sd: dict, cfg, ids: torch.Tensor) -> torch.Tensor:
         g = h @ f[p + "ffn.fused_linear_layer1.weight"].T
         u = h @ f[p + "ffn.linear_layerP.weight"].T
         x = x + (torch.nn.functional.silu(g) * u) @ f[p + "ffn.linear_layer2.weight"].T
+    if last_only:
+        x = x[:, -1:]
     x = O.rmsnorm(x, f["final_rmsnorm.weight"], 1e-6)
     return x @ f["out_head.weight"].T
 
@@ -45,6 +48,13 @@ def decode_step_cached(f: dict, cfg, tok: torch.Tensor, kc: list, vc: list, pos:
     """One greedy decode step with a KV cache (fp32 CPU): tok [B] at position
     `pos`; kc/vc per layer [B, Hkv, cap, D] are written at row pos.  Returns
     the next tokens [B].  Same arithmetic as forward() restricted to one row."""
+    return decode_logits_cached(f, cfg, tok, kc, vc, pos).argmax(-1)
+
+
+@torch.no_grad()
+def decode_logits_cached(f: dict, cfg, tok: torch.Tensor, kc: list, vc: list,
+                         pos: int) -> torch.Tensor:
+    """decode_step_cached's logits [B, V] (fp32) before the argmax."""
     B = tok.shape[0]
     Hq, Hkv, D = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     cos, sin = O.compute_rope_params(D, cfg.rope_base, pos + 1)
@@ -70,7 +80,7 @@ def decode_step_cached(f: dict, cfg, tok: torch.Tensor, kc: list, vc: list, pos:
         u = h @ f[p + "ffn.linear_layerP.weight"].T
         x = x + (torch.nn.functional.silu(g) * u) @ f[p + "ffn.linear_layer2.weight"].T
     x = O.rmsnorm(x, f["final_rmsnorm.weight"], 1e-6)
-    return (x[:, 0] @ f["out_head.weight"].T).argmax(-1)
+    return x[:, 0] @ f["out_head.weight"].T
 
 
 def random_state_dict(cfg, std: float = 0.02, seed: int = 0) -> dict:

@@ -41,7 +41,10 @@ def test_noalloc_matches_workspace_entry_point_twice(window):
         kc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16).cuda()
         vc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16).cuda()
         lens = [Smax - 7 * i - 300 * call for i in range(B)]
-        assert ops.decode_workspace_bytes(B, Hq, max(lens), D) > 0
+        # this exact shape (Hkv = 8, this window) sends its partials through
+        # the scratch array, not only through the cluster merge
+        assert N.lib().tpp_attention_decode_workspace_exact(B, Hq, Hkv, max(lens), D,
+                                                            window) > 0
         sl = torch.tensor(lens, dtype=torch.int32).cuda()
         ref = ops.attention_decode(q, kc, vc, sl, max(lens), window_left=window)
         out = torch.full_like(ref, float("nan"))

@@ -411,6 +411,15 @@ extern "C" int64_t tpp_attention_decode_workspace(int64_t B, int64_t Hq, int64_t
   return worst;
 }
 
+extern "C" int64_t tpp_attention_decode_workspace_exact(int64_t B, int64_t Hq, int64_t Hkv,
+                                                        int64_t max_seqlen, int64_t D,
+                                                        int64_t window_left) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || D <= 0 || max_seqlen <= 0) return 0;
+  int64_t range = max_seqlen;
+  if (window_left >= 0 && window_left + 1 < range) range = window_left + 1;
+  return attn_decode_workspace_bytes(B, Hq, Hkv, range, D);
+}
+
 extern "C" int tpp_attention_decode(const void* q, int64_t q_sb, int64_t q_sh,
                                     const void* k_cache, const void* v_cache, int64_t c_sb,
                                     int64_t c_sh, int64_t c_ss, const int32_t* seqlens,

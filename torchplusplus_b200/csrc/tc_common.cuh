@@ -49,8 +49,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // legitimate wait in these kernels.  On expiry the error flag is raised and
 // false is returned so the caller can wind down instead of hanging the GPU.
 constexpr uint32_t kWaitLimit = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint32_t limit = kWaitLimit) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicExch(err, code);
   return false;

@@ -70,6 +70,29 @@ int make_tmap(CUtensorMap* map, const void* base, int dtype, int rank, const uin
 
 }  // namespace tpp
 
+namespace {
+// The expiry path of mbar_wait, exercised on purpose: one thread waits on an
+// mbarrier that nothing arrives on and no copy completes on, with a short
+// poll limit; the wait gives up, raises the flag and the kernel returns.
+__global__ void bounded_wait_expiry_kernel(int* err, uint32_t polls, int code) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  tpp::mbar_init(&bar, 1);
+  tpp::fence_mbar_init();
+  tpp::mbar_wait(&bar, 0, err, code, polls);
+}
+}  // namespace
+
+extern "C" int tpp_debug_expire_wait(uint32_t polls, int code, void* stream) {
+  TPP_REQUIRE(polls > 0 && polls <= (1u << 16) && code != 0, TPP_ERR_SHAPE,
+              "polls must be in [1, 65536] and code nonzero");
+  int* err = tpp::device_error_flag();
+  TPP_REQUIRE(err != nullptr, TPP_ERR_LAUNCH, "device error flag unavailable");
+  bounded_wait_expiry_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(err, polls,
+                                                                                   code);
+  return tpp::check_launch("bounded_wait_expiry_kernel");
+}
+
 // Reads and clears the device-side error flag raised by bounded waits.
 extern "C" int tpp_device_error(void* stream) {
   int v = 0, zero = 0;
