@@ -1,0 +1,154 @@
+"""GPU comparator: the reference's own CUDA path for the Qwen3-0.6B-shaped
+decode, timed on the same B200 as this package's engine.
+
+It runs the unmodified reference installed under baseline/_ref (by
+baseline/install_ref.sh): torchpp's CUDA extensions built for sm_100a
+(rmsnormFused, ropeApplyFunction, linearActvationFp16, ...), its modules
+(RmsNormFused, GroupedQueryAttention with flash_attn_func, LinearSILU,
+nn.Linear on cuBLAS) and its model file examples/LLM/fastqwen3.py, fp16
+(the only dtype its kernels take).  The shipped example does not run as is;
+these patches make it run and change none of its kernels:
+
+0. torchpp/dlops/__init__.py and torchpp/attention/__init__.py fail to
+   import (they import their submodules as top-level modules, and
+   attention/xattention.py imports a `torchpp.utils` that does not exist);
+   both packages are registered without running those __init__ files, so
+   `torchpp.dlops.normalization`, `torchpp.attention.gqa`, ... import as files.
+1. `torchpp.dlops.fused_linear`, which fastqwen3.py:7 imports, does not exist
+   in the package; it is aliased to `torchpp.dlops.linear`, where LinearSILU
+   lives.
+2. FFN (fastqwen3.py:50-75) applies its 1024->3072 `linear_layerP` to the
+   3072-wide SiLU output, a shape error; the patched forward applies gate and
+   up to the FFN input: down(LinearSILU(x) * up(x)), same parameters.
+3. KVCache (torchpp/llmops/kvcache.py): `reset()` fails before the first
+   update and the append path returns a single slot (kvcache.py:76-79); the
+   replacement appends in place at any batch size and returns `.contiguous()`
+   copies of the valid prefix, the cost the reference's index path pays each
+   step (kvcache.py:106-107).
+4. LLMInference.generate (llm.py:226-286) calls token.item() each step, so it
+   runs only at batch 1; the timed loop issues the same forward calls with a
+   greedy argmax and keeps the per-step .item() at batch 1 only.
+
+LinearSILU's epilogue discards the accumulator (csrc/activation/
+fused_gemm.cuh:79-90), so its outputs are wrong and the generated tokens
+mean nothing: this is a timing-only comparator.
+
+Prints one JSON line: {"batch", "decode_tokens_per_s", "ms_per_step", ...}.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+REF = Path(__file__).resolve().parent / "_ref"
+
+
+def load_reference():
+    if not (REF / "torchpp").is_dir() or not (REF / "examples/LLM/fastqwen3.py").is_file():
+        raise RuntimeError("reference not installed under baseline/_ref "
+                           "(run baseline/install_ref.sh in the build container)")
+    sys.path.insert(0, str(REF))
+    import torchpp                                                    # patch 0
+    for sub in ("dlops", "attention"):
+        pkg = types.ModuleType(f"torchpp.{sub}")
+        pkg.__path__ = [str(REF / "torchpp" / sub)]
+        sys.modules[f"torchpp.{sub}"] = pkg
+        setattr(torchpp, sub, pkg)
+    import torchpp.dlops.linear as ref_linear
+    import torchpp.llmops.llm as ref_llm
+    sys.modules["torchpp.dlops.fused_linear"] = ref_linear          # patch 1
+    spec = importlib.util.spec_from_file_location("ref_fastqwen3",
+                                                  REF / "examples/LLM/fastqwen3.py")
+    fq = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(fq)
+
+    def ffn_forward(self, x):                                         # patch 2
+        return self.linear_layer2(self.fused_linear_layer1(x) * self.linear_layerP(x))
+    fq.FFN.forward = ffn_forward
+
+    class PrefixKVCache:                                              # patch 3
+        def __init__(self, max_seq_len, n_kv_heads, head_dim, dtype=torch.float16,
+                     device=torch.device("cuda")):
+            self.max_seq_len, self.n_kv_heads, self.head_dim = max_seq_len, n_kv_heads, head_dim
+            self.dtype, self.device = dtype, device
+            self.k_cache = self.v_cache = None
+            self.cache_len = 0
+
+        def update(self, k, v, index=None):
+            B, H, s, D = k.shape
+            if self.k_cache is None or self.k_cache.shape[0] != B:
+                self.k_cache = torch.zeros(B, H, self.max_seq_len, D, dtype=self.dtype,
+                                           device=self.device)
+                self.v_cache = torch.zeros_like(self.k_cache)
+            start = self.cache_len if index is None else index
+            self.k_cache[:, :, start:start + s] = k
+            self.v_cache[:, :, start:start + s] = v
+            self.cache_len = max(self.cache_len, start + s)
+            return (self.k_cache[:, :, :self.cache_len].contiguous(),
+                    self.v_cache[:, :, :self.cache_len].contiguous())
+
+        def reset(self):
+            self.cache_len = 0
+    ref_llm.KVCache = PrefixKVCache
+    return fq
+
+
+@torch.inference_mode()
+def run(batch: int, prompt: int, gen: int, seed: int = 0) -> dict:
+    fq = load_reference()
+    torch.manual_seed(seed)
+    cfg = fq.QwenConfig_float16()
+    model = fq.FastQwen3(cfg).to("cuda")
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    for _, p in model.named_parameters():
+        if p.dim() >= 2:
+            p.copy_((torch.randn(p.shape, generator=g, device="cuda") * 0.02).to(p.dtype))
+        else:
+            p.fill_(1.0)
+    ids = torch.randint(0, cfg.vocab_size, (batch, prompt), generator=g, device="cuda")
+
+    def request(timed: bool):
+        model.setup_kv_cache(prompt + gen)
+        model.reset_kv_cache()
+        logits = model.forward(ids, use_cache=True, cache_position=0)
+        tok = logits[:, -1, :].argmax(-1, keepdim=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(gen - 1):
+            logits = model.forward(tok, use_cache=True, cache_position=prompt + i)
+            tok = logits[:, -1, :].argmax(-1, keepdim=True)
+            if batch == 1:
+                model._should_stop(tok, [], None)       # the stock loop's per-step sync
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 1e3
+
+    request(False)
+    t = request(True)
+    return {"batch": batch, "prompt": prompt, "gen": gen, "dtype": "f16",
+            "decode_tokens_per_s": batch * (gen - 1) / t, "ms_per_step": t / (gen - 1) * 1e3,
+            "path": "torchpp CUDA extensions (sm_100a) + flash_attn_func + cuBLAS nn.Linear, "
+                    "eager, examples/LLM/fastqwen3.py with 5 documented patches"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=256)
+    a = ap.parse_args()
+    try:
+        print(json.dumps(run(a.batch, a.prompt, a.gen)), flush=True)
+    except Exception as e:  # noqa: BLE001 - reported, not raised: the bench goes on
+        print(json.dumps({"batch": a.batch, "unavailable": f"{type(e).__name__}: {e}"}),
+              flush=True)
+
+
+if __name__ == "__main__":
+    main()

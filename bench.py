@@ -40,6 +40,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tokens/sec (Qwen3-0.6B shape) at 1/2/4/8 B200; per-op % of HBM/TC roofline"
 PROMPT, GEN = 512, 256
+# The CPU sample decodes at the middle of the GPU arm's context span
+# (513..767): its per-token cost grows with the context, so the mean context
+# stands in for the whole span.
+CPU_CTX = PROMPT + GEN // 2 - 2
 
 
 # Measured DRAM traffic of the decode linears (ncu dram__bytes_read.sum +
@@ -162,7 +166,7 @@ def cpu_decode_rate(batch: int, steps: int, ctx: int, threads: int | None = None
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    b = cpu_decode_rate(args.batch, args.cpu_steps, PROMPT)
+    b = cpu_decode_rate(args.batch, args.cpu_steps, CPU_CTX)
     line = {"impl": "reference", "metric": METRIC, "value": b["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -496,6 +500,96 @@ def one_op(name: str, reps: int) -> dict:
     return {"one_op": name, "reps": reps, "us_per_rep": e0.elapsed_time(e1) * 1e3 / reps}
 
 
+def torchpp_comparator(model, prompt_ids, cap: int, nrep: int) -> dict:
+    """The reference's own CUDA decode path (baseline/torchpp_gpu.py: torchpp's
+    sm_100a extensions + flash_attn + cuBLAS, fp16, eager) at batch 1 and 32,
+    run in a subprocess on this GPU, next to this engine on the same fp16
+    model shape and decode length."""
+    from torchplusplus_b200.llmops.qwen3 import Qwen3, Qwen3Config
+    out = {}
+    for bsz in (1, 32):
+        try:
+            r = subprocess.run([sys.executable, str(ROOT / "baseline" / "torchpp_gpu.py"),
+                                "--batch", str(bsz), "--prompt", str(PROMPT), "--gen", str(GEN)],
+                               capture_output=True, text=True, timeout=600,
+                               env={**os.environ, "CUDA_VISIBLE_DEVICES":
+                                    os.environ.get("CUDA_VISIBLE_DEVICES", "0")})
+            lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+            out[f"torchpp_cuda_batch{bsz}"] = json.loads(lines[-1]) if lines else \
+                {"unavailable": (r.stderr or "no output").strip().splitlines()[-1][:300]}
+        except (subprocess.TimeoutExpired, OSError) as e:
+            out[f"torchpp_cuda_batch{bsz}"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    # this engine on the same fp16 model (the reference's kernels are fp16-only)
+    m16 = Qwen3(Qwen3Config(dtype=torch.float16),
+                device=model.out_head.weight.device).init_weights(0.02, seed=0)
+    for bsz in (1, 32):
+        e = m16.engine(bsz, cap)
+        e.prefill(prompt_ids[:bsz])
+        e.capture()
+        e.decode(8)
+        e.prefill(prompt_ids[:bsz])
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        e.decode(nrep)
+        a1.record()
+        a1.synchronize()
+        out[f"ours_f16_batch{bsz}_decode_tokens_per_s"] = bsz * nrep / (a0.elapsed_time(a1) / 1e3)
+        m16._engine = None
+    for bsz in (1, 32):
+        ref = out[f"torchpp_cuda_batch{bsz}"].get("decode_tokens_per_s")
+        if ref:
+            out[f"ratio_batch{bsz}"] = out[f"ours_f16_batch{bsz}_decode_tokens_per_s"] / ref
+    del m16
+    torch.cuda.empty_cache()
+    return out
+
+
+def strong_scaling(model, prompt_ids, cap: int, nrep: int, world: int) -> dict:
+    """Fixed global work split over the ranks (no collective): the decode at
+    global batch 32 (32 / N sequences per GPU) and the SWA decode attention at
+    global batch 64 (64 / N per GPU, cache length 16384, window 4096).
+    Aggregate throughput = global work / max-over-ranks device time."""
+    from torchplusplus_b200 import ops
+    out = {}
+    bs = max(1, 32 // world)
+    e = model.engine(bs, cap)
+    e.prefill(prompt_ids[:bs])
+    e.capture()
+    e.decode(8)
+    e.prefill(prompt_ids[:bs])
+    torch.cuda.synchronize()
+    barrier(world)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    e.decode(nrep)
+    a1.record()
+    a1.synchronize()
+    t = max_over_ranks(a0.elapsed_time(a1) / 1e3, world)
+    out["decode_global_batch32"] = {"per_gpu_batch": bs, "tokens_per_s": bs * world * nrep / t,
+                                    "ms_per_decode_step": t / nrep * 1e3}
+    model._engine = None
+    del e
+    B, L = max(1, 64 // world), 16384
+    g = torch.Generator(device="cuda").manual_seed(7)
+    kc = torch.randn(B, 8, L, 128, generator=g, device="cuda", dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(B, 16, 128, generator=g, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    ws = torch.empty(max(16, ops.decode_workspace_bytes(B, 16, L, 128)), dtype=torch.uint8,
+                     device="cuda")
+    barrier(world)
+    t = max_over_ranks(_time_graph([lambda: ops.attention_decode(
+        q, kc, vc, sl, L, window_left=4095, out=o, workspace=ws)] * 10) / 10, world)
+    nb = B * world * (2 * 4096 * 8 * 128 * 2 + 2 * 16 * 128 * 2)
+    out["swa_decode_global_batch64_L16384"] = {"per_gpu_batch": B, "us": t * 1e6,
+                                               "aggregate_GBps": nb / t / 1e9}
+    del kc, vc
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local):
     from torchplusplus_b200 import _native as N
     from torchplusplus_b200.llmops.qwen3 import Qwen3, Qwen3Config
@@ -609,6 +703,10 @@ def run_ours(args, rank, world, local):
             model._engine = None
             del ef
 
+    if not args.skip_strong:
+        extra["strong_scaling"] = strong_scaling(model, prompts[0], cap, nrep, world)
+    if rank == 0 and not args.skip_torchpp:
+        extra["gpu_comparator"] = torchpp_comparator(model, prompts[0], cap, nrep)
     lps = eng.launches_per_step or 0
     ops_res = None
     if rank == 0 and not args.skip_ops:
@@ -621,7 +719,7 @@ def run_ours(args, rank, world, local):
         ops_res = per_op(peak, float(peaks_d.get("bf16_tflops", 1590.0)))
     if rank != 0:
         return
-    cpu = cpu_decode_rate(B, args.cpu_steps, PROMPT) if world == 1 and not args.skip_cpu else None
+    cpu = cpu_decode_rate(B, args.cpu_steps, CPU_CTX) if world == 1 and not args.skip_cpu else None
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": tmax / args.steps * 1e3, "higher_is_better": True,
@@ -653,6 +751,10 @@ def main():
     ap.add_argument("--skip-b1", action="store_true")
     ap.add_argument("--skip-ops", action="store_true", help="skip the per-op roofline table")
     ap.add_argument("--skip-fp8", action="store_true", help="skip the fp8-weights decode lines")
+    ap.add_argument("--skip-strong", action="store_true",
+                    help="skip the fixed-global-batch (strong scaling) lines")
+    ap.add_argument("--skip-torchpp", action="store_true",
+                    help="skip the reference's CUDA-path comparator (baseline/torchpp_gpu.py)")
     ap.add_argument("--gen", type=int, default=GEN,
                     help="tokens generated per request (profiling runs use fewer)")
     ap.add_argument("--one-op", default=None, choices=ONE_OPS,

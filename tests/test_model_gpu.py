@@ -51,7 +51,11 @@ def test_prefill_logits_match_oracle_model(dtype):
     err = (got - ref).abs()
     scale = ref.abs().max().item()
     assert err.max().item() <= 2e-2 * max(1.0, scale), (err.max().item(), scale)
-    assert err.mean().item() <= 1e-2 * max(1.0, ref.abs().mean().item())
+    # mean: no further from the fp32 oracle than the same formulation run
+    # eagerly in the model's dtype (every module output stored in it), the
+    # bar of tests/test_bench_shapes_gpu.py
+    ref16 = OM.forward(m.state_dict(), m.cfg, ids, store_dtype=dtype)
+    assert err.mean().item() <= 1.25 * (ref16 - ref).abs().mean().item() + 1e-3
 
 
 def test_cached_decode_matches_full_forward():
