@@ -19,7 +19,8 @@ these patches make it run and change none of its kernels:
    lives.
 2. FFN (fastqwen3.py:50-75) applies its 1024->3072 `linear_layerP` to the
    3072-wide SiLU output, a shape error; the patched forward applies gate and
-   up to the FFN input: down(LinearSILU(x) * up(x)), same parameters.
+   up to the FFN input: down(LinearSILU(x) * up(x)), same parameters, with x
+   flattened to 2-D for LinearSILU, whose binding rejects 3-D input.
 3. KVCache (torchpp/llmops/kvcache.py): `reset()` fails before the first
    update and the append path returns a single slot (kvcache.py:76-79); the
    replacement appends in place at any batch size and returns `.contiguous()`
@@ -69,7 +70,9 @@ def load_reference():
     spec.loader.exec_module(fq)
 
     def ffn_forward(self, x):                                         # patch 2
-        return self.linear_layer2(self.fused_linear_layer1(x) * self.linear_layerP(x))
+        # the LinearSilu binding takes 2-D input only (csrc/activation/binding.cu:65)
+        g = self.fused_linear_layer1(x.reshape(-1, x.shape[-1])).view(*x.shape[:-1], -1)
+        return self.linear_layer2(g * self.linear_layerP(x))
     fq.FFN.forward = ffn_forward
 
     class PrefixKVCache:                                              # patch 3

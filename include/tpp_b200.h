@@ -56,15 +56,6 @@ const char* tpp_last_error(void);
 const char* tpp_version(void);
 /* Number of kernel launches this library has issued in the calling process. */
 uint64_t tpp_launch_count(void);
-/* L2 prefetch hint for the next launch from the calling host thread: when
- * that launch is a decode linear (tpp_linear / tpp_rmsnorm_linear on the
- * x-stationary path) or a decode attention (tpp_attention_decode*), its CTAs
- * each prefetch their share of [p, p + bytes) into L2 after issuing their own
- * first loads; any other launch drops the hint.  Meant for a dependent chain
- * whose next kernel's weights are known (the decode step), so they stream
- * from HBM under the current kernel.  p 16-byte aligned; bytes 0 clears.
- * No reference counterpart (the reference launches eagerly). */
-int tpp_l2_prefetch_hint(const void* p, int64_t bytes);
 /* Reads and clears (synchronising `stream`) the current device's error flag,
  * which a kernel sets when one of its bounded device-side waits runs out
  * instead of spinning forever.  Returns 0 if no wait expired, the nonzero

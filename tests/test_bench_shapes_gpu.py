@@ -117,6 +117,7 @@ def test_config4_engine_prefill_and_decode_match_oracle(qwen3_0p6b, weight_forma
     ref16 = OM.forward(sd, cfg, ids[ROWS], last_only=True, store_dtype=torch.bfloat16)[:, 0]
     _check_model(pre, ref, ref16, "prefill logits")
     # teacher-forced decode steps from the engine's cache and tokens
+    kc, vc = [t.clone() for t in kc], [t.clone() for t in vc]     # writable outside inference
     kc16, vc16 = [t.clone() for t in kc], [t.clone() for t in vc]
     for t, lg in enumerate(steps):
         pos = 512 + t

@@ -32,8 +32,6 @@ struct DecMmaArgs {
   // [num_blocks][Hkv][64][D]; key k of sequence b lives in block
   // table[b * tbl_stride + k / 64], row k % 64.
   const int32_t* table; int64_t tbl_stride; int64_t num_blocks;
-  // L2 prefetch hint (the next kernel's operands), spread over the CTAs
-  const void* pf; int64_t pf_bytes;
 #ifdef TPP_DEBUG_STAMPS
   unsigned dbg_id;
 #endif

@@ -164,10 +164,6 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
   if (tid == 0) {
     for (int i = 0; i < ntiles && i < kStages; ++i) issue(i);
   }
-  if (warp == 1)
-    l2_prefetch_share(p.pf, p.pf_bytes,
-                      ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
-                      (int64_t)gridDim.x * gridDim.y * gridDim.z, lane, 32);
   // fused mode: the static RoPE tables and norm weights load before the wait
   constexpr int EPL = D / 32;
   float cv[EPL], sv[EPL], wq[EPL], wk[EPL];
@@ -639,11 +635,6 @@ int decode_mma_launch(DecMmaArgs& a, const void* k_cache, const void* v_cache, i
 #ifdef TPP_DEBUG_STAMPS
   a.dbg_id = g_dec_launch++;
 #endif
-  {
-    const L2Hint h = take_l2_hint();
-    a.pf = h.p;
-    a.pf_bytes = h.bytes;
-  }
   CUtensorMap tk, tv;
   const uint64_t smax = (uint64_t)(a.max_seqlen > 0 ? a.max_seqlen : 1);
   // {64 columns, key, column box (D/64), kv head, batch}: the tile's column

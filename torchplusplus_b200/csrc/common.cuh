@@ -139,43 +139,6 @@ __device__ __forceinline__ void pdl_trigger() {
 // PDL on unless the environment sets TPP_PDL=0 (for A/B measurements).
 bool pdl_enabled();
 
-// ---------------------------------------------------------------------------
-// L2 prefetch hint.  A caller that knows which weights the NEXT kernel of a
-// dependent chain will stream (the decode step) names them before launching
-// the current kernel (tpp_l2_prefetch_hint); launchers that support it take
-// the hint into the kernel's arguments, and the kernel's CTAs each issue
-// bulk L2 prefetches for their share of the range right after their own
-// first loads.  Those bytes then move while HBM would otherwise idle (launch
-// gaps, prologues, epilogues) and the next kernel reads them from L2.  The
-// hint is per host thread and is consumed (or dropped) by the next launch.
-// ---------------------------------------------------------------------------
-struct L2Hint {
-  const void* p = nullptr;
-  int64_t bytes = 0;
-};
-L2Hint take_l2_hint();
-void clear_l2_hint();
-
-// This CTA's share (cta of nctas, 256-byte aligned parts) of [base, base +
-// bytes) prefetched into L2 by `nl` lanes (lane = 0 .. nl-1), in bulk
-// requests of up to 16 KB (whole 16-byte units; a ragged tail is skipped).
-__device__ __forceinline__ void l2_prefetch_share(const void* base, int64_t bytes, int64_t cta,
-                                                  int64_t nctas, int lane, int nl) {
-  if (base == nullptr || bytes <= 0 || nctas <= 0) return;
-  constexpr int64_t kChunk = 16 * 1024;
-  int64_t per = (bytes + nctas - 1) / nctas;
-  per = (per + 255) & ~(int64_t)255;
-  const int64_t s = cta * per;
-  const int64_t e = s + per < bytes ? s + per : bytes;
-  const char* b = static_cast<const char*>(base);
-  for (int64_t off = s + (int64_t)lane * kChunk; off < e; off += (int64_t)nl * kChunk) {
-    const int64_t n = (e - off < kChunk ? e - off : kChunk) & ~(int64_t)15;
-    if (n > 0)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b + off), "r"((uint32_t)n)
-                   : "memory");
-  }
-}
-
 template <typename... KArgs, typename... Args>
 int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
            cudaStream_t st, unsigned cluster_y, Args&&... args) {
@@ -201,7 +164,6 @@ int launch(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size
   cfg.attrs = attr;
   cfg.numAttrs = n;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-  clear_l2_hint();
   if (e != cudaSuccess) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
     return TPP_ERR_LAUNCH;

@@ -85,9 +85,6 @@ struct XsArgs {
   uint8_t* ypk;
   // fp8 weights (W8 variant): per-row dequantisation scales [N] (SwiGLU: [2N])
   const float* wscale;
-  // L2 prefetch hint (the next kernel's weights), spread over the CTAs
-  const void* pf;
-  int64_t pf_bytes;
 #ifdef TPP_DEBUG_STAMPS
   unsigned dbg_id;
 #endif
@@ -216,6 +213,7 @@ __global__ void __launch_bounds__(xs_threads(NTM), NTM > 4 ? 1 : (BN == 16 ? 3 :
 
   if (warp == KW) {
     // ---------------- TMA / bulk producer ----------------
+    if (lane != 0) return;
     bool ok = true;
     auto kbc = [&](int c) { return nkb - c * KC < KC ? nkb - c * KC : KC; };
     auto tx_bytes = [&](int c) {
@@ -247,22 +245,15 @@ __global__ void __launch_bounds__(xs_threads(NTM), NTM > 4 ? 1 : (BN == 16 ? 3 :
       else
         tma_load_3d(dst, &tm_x, &full[c % S], 0, t0, c * KC);
     };
+    XS_TS(4);
+    if (!p.wpk) prefetch_tmap(&tm_w);
+    if (!p.xpk) prefetch_tmap(&tm_x);
+    XS_TS(5);
     const int pre = NCH < S ? NCH : S;
-    if (lane == 0) {
-      XS_TS(4);
-      if (!p.wpk) prefetch_tmap(&tm_w);
-      if (!p.xpk) prefetch_tmap(&tm_x);
-      XS_TS(5);
-      for (int c = 0; c < pre; ++c) {
-        mbar_arrive_expect_tx(&full[c], tx_bytes(c));
-        load_w(c);  // weights: independent of the previous kernel
-      }
+    for (int c = 0; c < pre; ++c) {
+      mbar_arrive_expect_tx(&full[c], tx_bytes(c));
+      load_w(c);  // weights: independent of the previous kernel
     }
-    __syncwarp();
-    // the next kernel's weights, behind this CTA's own first requests
-    l2_prefetch_share(p.pf, p.pf_bytes, (int64_t)blockIdx.y * gridDim.x + blockIdx.x,
-                      (int64_t)gridDim.x * gridDim.y, lane, 32);
-    if (lane != 0) return;
     XS_TS(12);
     pdl_wait();
     XS_TS(13);
@@ -1134,11 +1125,6 @@ int linear_xs_impl(const void* x, int64_t ldx, const void* w, const void* bias,
   a.xpk = static_cast<const uint8_t*>(xpk);
   a.ypk = static_cast<uint8_t*>(ypk);
   a.wscale = nullptr;
-  {
-    const L2Hint h = take_l2_hint();
-    a.pf = h.p;
-    a.pf_bytes = h.bytes;
-  }
   return TPP_DISPATCH_HALF(dtype, T, [&] {
     return norm_eps >= 0.f ? xs_dispatch<T, true>(x, ldx, w, a, dtype, st, L)
                            : xs_dispatch<T, false>(x, ldx, w, a, dtype, st, L);
@@ -1182,11 +1168,6 @@ int linear_xs_fp8(const void* x, int64_t ldx, const void* q, const float* scale,
   a.err = device_error_flag();
   a.wpk = nullptr; a.xpk = nullptr; a.ypk = nullptr;
   a.wscale = scale;
-  {
-    const L2Hint h = take_l2_hint();
-    a.pf = h.p;
-    a.pf_bytes = h.bytes;
-  }
   if (wide)
     return TPP_DISPATCH_HALF(dtype, T, [&] {
       if (bnw == 16)

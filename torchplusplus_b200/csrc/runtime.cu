@@ -8,15 +8,7 @@ namespace tpp {
 static thread_local std::string g_last_error;
 static std::atomic<uint64_t> g_launches{0};
 
-static thread_local L2Hint g_l2_hint;
-
 void set_error(const std::string& msg) { g_last_error = msg; }
-L2Hint take_l2_hint() {
-  const L2Hint h = g_l2_hint;
-  g_l2_hint = L2Hint{};
-  return h;
-}
-void clear_l2_hint() { g_l2_hint = L2Hint{}; }
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 bool pdl_enabled() {
@@ -42,12 +34,3 @@ int check_launch(const char* what) {
 extern "C" const char* tpp_last_error(void) { return tpp::g_last_error.c_str(); }
 extern "C" const char* tpp_version(void) { return "tpp_b200 0.1 (sm_100a)"; }
 extern "C" uint64_t tpp_launch_count(void) { return tpp::g_launches.load(); }
-extern "C" int tpp_l2_prefetch_hint(const void* p, int64_t bytes) {
-  if (bytes < 0 || (bytes > 0 && (reinterpret_cast<uintptr_t>(p) & 15u))) {
-    tpp::set_error("tpp_l2_prefetch_hint: the range must start on a 16-byte boundary");
-    return TPP_ERR_ALIGN;
-  }
-  tpp::g_l2_hint.p = bytes > 0 ? p : nullptr;
-  tpp::g_l2_hint.bytes = bytes;
-  return TPP_OK;
-}

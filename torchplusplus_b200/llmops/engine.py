@@ -18,7 +18,6 @@ cache per step (kvcache.py:106-107) and synchronises on token.item()
 """
 from __future__ import annotations
 
-import os
 from typing import List, Optional
 
 import torch
@@ -113,11 +112,6 @@ class DecodeEngine:
         # batch 32 -- the fork costs the chain its programmatic launch edge
         # and the prefetches compete with the K/V stream).
         self.l2_warm = False
-        # Each kernel of the step prefetches the NEXT projection's weights
-        # into L2 (tpp_l2_prefetch_hint): attention -> o-proj, o-proj ->
-        # gate/up, gate/up -> down, down -> next layer's qkv, embedding ->
-        # layer 0's qkv.  TPP_L2_HINT=0 turns it off (A/B measurements).
-        self.l2_hints = os.environ.get("TPP_L2_HINT", "1") != "0"
         # None = greedy; else dict(temperature, top_k, top_p, seed) (set_sampling)
         self.sampling: Optional[dict] = None
         self._graph_sampling: Optional[dict] = None
@@ -150,10 +144,8 @@ class DecodeEngine:
     def _step_lane(self, ln: dict, warm: Optional[torch.cuda.Stream] = None) -> None:
         n, Hq, Hkv, D = ln["n"], self.Hq, self.Hkv, self.D
         x = ln["x"]
-        hint = (lambda w: ops.l2_prefetch_hint(w)) if self.l2_hints else (lambda w: None)
         ops.embedding(ln["tokens"], self.emb, out=x)
-        nxt = self.layers[1:] + [None]
-        for L, Ln, kc, vc in zip(self.layers, nxt, ln["k"], ln["v"]):
+        for L, kc, vc in zip(self.layers, ln["k"], ln["v"]):
             f8 = L.get("f8")
             if f8 is not None:
                 ops.linear_fp8(x, f8["qkv"], eps=self.eps, out=ln["qkv"].view(n, -1))
@@ -169,8 +161,6 @@ class DecodeEngine:
                     for w in (L["wo"], L["wgu_f"], L["wdown"]):
                         ops.l2_prefetch(w)
             if self.fuse_qk_attention:
-                if f8 is None:
-                    hint(L["wo"])
                 ops.attention_decode_qkv(ln["qkv"], L["qn"], L["kn"], self.eps, self.cos,
                                          self.sin, ln["positions"], kc, vc, ln["seqlens"],
                                          self.max_seq_len, Hq, Hkv, out=ln["o"],
@@ -186,12 +176,8 @@ class DecodeEngine:
                 ops.linear_fp8(x, f8["gu"], eps=self.eps, out=ln["ff"])
                 ops.linear_fp8(ln["ff"], f8["down"], residual=x, out=x)
             else:
-                hint(L["wgu_f"])
                 ops.linear(ln["o"].view(n, Hq * D), L["wo"], residual=x, out=x)
-                hint(L["wdown"])
                 ops.rmsnorm_linear(x, L["wgu_f"], self.eps, act="swiglu", out=ln["ff"])
-                if Ln is not None and Ln.get("f8") is None:
-                    hint(Ln["wqkv_f"])
                 ops.linear(ln["ff"], L["wdown"], residual=x, out=x)
         if self.lm_head_f8 is not None:
             ops.linear_fp8(x, self.lm_head_f8, eps=self.eps, out=ln["logits"])

@@ -350,20 +350,6 @@ def l2_prefetch(t: torch.Tensor) -> None:
     N.call("tpp_l2_prefetch", t.data_ptr(), n - n % 16, N.stream_of(t))
 
 
-def l2_prefetch_hint(t: torch.Tensor | None) -> None:
-    """Names the weights the kernel AFTER the next launch will stream: the next
-    decode linear or decode attention launched from this thread prefetches
-    them into L2, spread over its CTAs (tpp_l2_prefetch_hint).  Any other
-    launch drops the hint; None clears it."""
-    if t is None:
-        N.call("tpp_l2_prefetch_hint", None, 0)
-        return
-    _cuda(t)
-    if not t.is_contiguous():
-        raise ValueError("l2_prefetch_hint needs a contiguous tensor")
-    N.call("tpp_l2_prefetch_hint", t.data_ptr(), t.numel() * t.element_size())
-
-
 def hgemv(weight: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """y[N] = weight[N,K] @ x[K] with fp32 accumulation."""
     _cuda(weight, x)
