@@ -416,6 +416,57 @@ def test_attention_decode_qkv_fused(dtype, case):
     check(y, y2.float().cpu())
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("case", [(32, 300), (4, 2000), (1, 9000)])   # (B, L): few .. many splits
+@pytest.mark.parametrize("fused", [False, True])
+def test_attention_decode_rising_scores(dtype, case, fused):
+    """Scores that rise steadily along the key range (key j aligned with q,
+    scaled by 40 j / L): each tile raises the row maximum a little, so the
+    lazy O rescale (base kept until the maximum grows by more than 2^8) and
+    the per-warp / per-split merges see stale bases grow step by step; the
+    new key of the fused mode carries the largest score."""
+    B, L = case
+    Hq, Hkv, D = 16, 8, 128
+    G = Hq // Hkv
+    g = gen(61)
+    cos, sin = O.compute_rope_params(D, 1e6, L + 1)
+    qraw = torch.randn(B, 1, Hq + 2 * Hkv, D, generator=g)
+    pos = torch.full((B,), L - 1, dtype=torch.int32)
+    # direction each kv head's keys align with: its first query head, as the
+    # kernel sees it (rotated at the new position in fused mode)
+    qdir = O.qk_norm_rope(qraw[:, :, :Hq], None, 1e-6, cos, sin, pos[:, None, None])[:, 0] \
+        if fused else qraw[:, 0, :Hq]
+    qdir = qdir[:, ::G]                                                   # [B, Hkv, D]
+    coef = 40.0 * torch.arange(L).float() / L * math.sqrt(D)              # score ~ 40 j / L
+    kc0 = coef[None, None, :, None] * (qdir / qdir.norm(dim=-1, keepdim=True) ** 2)[:, :, None]
+    kc0 = (kc0 + 0.3 * torch.randn(B, Hkv, L, D, generator=g)).to(dtype)
+    vc0 = torch.randn(B, Hkv, L, D, generator=g).to(dtype)
+    sl = torch.full((B,), L, dtype=torch.int32)
+    kc, vc = kc0.to(DEV), vc0.to(DEV)
+    if fused:
+        # the new key continues the ramp: raw k = the ramp's next row
+        qkv = qraw.clone()
+        qkv[:, 0, Hq:Hq + Hkv] = kc0[:, :, L - 1].float()
+        qkv = qkv.to(dtype)
+        y = ops.attention_decode_qkv(qkv.view(B, 1, -1).to(DEV), None, None, 1e-6, cos.to(DEV),
+                                     sin.to(DEV), pos.to(DEV), kc, vc, sl.to(DEV), L, Hq, Hkv)
+        x = qkv.view(B, 1, Hq + 2 * Hkv, D)
+        qref = O.qk_norm_rope(x[:, :, :Hq], None, 1e-6, cos, sin, pos[:, None, None])[:, 0]
+        kref = O.qk_norm_rope(x[:, :, Hq:Hq + Hkv], None, 1e-6, cos, sin, pos[:, None, None])
+        kr, vr = kc0.float().clone(), vc0.float().clone()
+        kr[:, :, L - 1] = kref[:, 0].to(dtype).float()
+        vr[:, :, L - 1] = x[:, 0, Hq + Hkv:].float()
+        ref = O.attention_decode(qref.to(dtype), kr.to(dtype), vr.to(dtype), sl)
+    else:
+        q = qraw[:, 0, :Hq].to(dtype)
+        y = ops.attention_decode(q.to(DEV), kc, vc, sl.to(DEV), L)
+        ref = O.attention_decode(q, kc0, vc0, sl)
+    check(y, ref)
+    if B == 1:   # the many-split case really goes through the split merge
+        from torchplusplus_b200 import _native as N
+        assert N.lib().tpp_attention_decode_workspace_exact(B, Hq, Hkv, L, D, -1) > 0
+
+
 def test_kv_append_and_kvcache():
     from torchplusplus_b200.llmops.kvcache import KVCache
     g = gen(15)

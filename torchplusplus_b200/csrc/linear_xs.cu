@@ -3,12 +3,12 @@
 //
 // At decode the weights are read once per step and M is a handful of tokens.
 // Two measured B200 facts shape this kernel:
-//  * A tcgen05.mma costs ~180 SM clocks whatever its shape (M64 x N8 as much
-//    as M128 x N256), so with 32 tokens on one side the 5th-generation path
-//    runs at 1/8 of its rate and a CTA's chain of K/16 MMAs becomes the
-//    critical path.  Warp-level mma.sync m16n8k16 sustains ~1000 FMA/clock/SM
-//    from four warps with cost proportional to the work: ~3x faster for these
-//    tiles.  (Large GEMMs stay on tcgen05 in linear_tc.cu.)
+//  * Back-to-back tcgen05.mma instructions never cost less than ~52 SM clocks
+//    each for N <= 64 (a single one's latency is ~390), so with 32 tokens on
+//    one side the 5th-generation path sustains ~1250 FMA/clock/SM, about
+//    what warp-level mma.sync m16n8k16 gives (~1000 FMA/clock/SM from four
+//    warps) without TMEM traffic or a single issuing thread.  (Large GEMMs
+//    stay on tcgen05 in linear_tc.cu.)
 //  * A CTA's TMA throughput is set by its number of requests (~0.2 us each)
 //    more than by their size, so operands arrive in few large chunks.
 // Design:
