@@ -24,6 +24,7 @@
 // csrc/activation/fused_gemm.cuh:143-170 (mma.sync 16x8x16, 128x128x32 tiles,
 // activation epilogue at fused_gemm.cuh:79-105 whose accumulator conversion is
 // missing); parity here is against the PyTorch formula act(x W^T + b).
+#include <stdlib.h>
 #include "tc_common.cuh"
 
 namespace tpp {
@@ -34,17 +35,27 @@ constexpr int BK = 64;  // 128 bytes of fp16/bf16: one swizzle row
 constexpr int kThreads = 384;
 constexpr int kEpiWarp0 = 4;
 constexpr int kEpiThreads = 256;
-constexpr uint32_t kStageA = BM * BK * 2;  // 16 KB
+#ifndef TPP_TC_BN2
+#define TPP_TC_BN2 192
+#endif
+constexpr uint32_t kSubA = BM * BK * 2;  // one 64-wide k-block of x: 16 KB
 
-template <bool SWIGLU>
+// KS k-blocks per ring stage.  A stage's operands arrive as ONE TMA request
+// each (a 3-D / 4-D box spanning KS k-blocks): a CTA's TMA issue rate, not
+// the bytes, bounds the feed at these tile sizes, so KS = 2 halves the
+// requests per tile (KS = 1 serves K not a multiple of 64, with 2-D maps).
+template <bool SWIGLU, int KS>
 struct TcCfg {
-  static constexpr int BN = SWIGLU ? 256 : 192;       // MMA N (accumulator columns)
+  static constexpr int BN = SWIGLU ? 256 : (KS == 2 ? TPP_TC_BN2 : 192);  // MMA N
   static constexpr int NOUT = SWIGLU ? BN / 2 : BN;   // output columns per tile
-  static constexpr int kStages = SWIGLU ? 3 : 4;
-  static constexpr uint32_t kStageB = BN * BK * 2;
+  static constexpr int kStages = KS == 2 ? (SWIGLU || BN > 128 ? 2 : 3) : (SWIGLU ? 3 : 4);
+  static constexpr uint32_t kSubB = BN * BK * 2;      // one k-block of W
+  static constexpr uint32_t kStageA = KS * kSubA;
+  static constexpr uint32_t kStageB = KS * kSubB;
   static constexpr uint32_t kOut = BM * NOUT * 2;     // staged output tile
   static constexpr size_t kSmem =
       (size_t)kStages * (kStageA + kStageB) + kOut + 1024 /*align*/ + 256 /*bars*/;
+  static_assert(kSmem <= 227 * 1024, "shared memory plan exceeds 227 KB");
 };
 
 struct TcArgs {
@@ -62,19 +73,19 @@ __device__ __forceinline__ void epi_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
 }
 
-template <typename T, bool SWIGLU>
+template <typename T, bool SWIGLU, int KS>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_y, TcArgs p) {
-  using C = TcCfg<SWIGLU>;
+  using C = TcCfg<SWIGLU, KS>;
   constexpr int BN = C::BN, NOUT = C::NOUT, S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: the 128B-swizzle pattern repeats every 8 rows of 128 B.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * kStageA;
+  uint8_t* sB = smem + S * C::kStageA;
   uint8_t* sout = sB + S * C::kStageB;
   uint64_t* full = reinterpret_cast<uint64_t*>(sout + C::kOut);
   uint64_t* empty = full + S;
@@ -85,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntm = (p.M + BM - 1) / BM;
   const int ntiles = ntm * ((p.N + NOUT - 1) / NOUT);
-  const int nk = (p.K + BK - 1) / BK;
+  const int nk = (p.K + BK * KS - 1) / (BK * KS);  // ring stages per tile
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tm_x);
@@ -121,13 +132,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = it % S;
         if (it >= S) ok = mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.err, 1);
         if (!ok) break;
-        mbar_arrive_expect_tx(&full[s], kStageA + C::kStageB);
-        tma_load_2d(sA + s * kStageA, &tm_x, &full[s], kb * BK, m0);
-        if (SWIGLU) {
-          tma_load_2d(sB + s * C::kStageB, &tm_w, &full[s], kb * BK, n0);
-          tma_load_2d(sB + s * C::kStageB + C::kStageB / 2, &tm_w, &full[s], kb * BK, p.N + n0);
+        mbar_arrive_expect_tx(&full[s], C::kStageA + C::kStageB);
+        if constexpr (KS == 1) {
+          tma_load_2d(sA + s * C::kStageA, &tm_x, &full[s], kb * BK, m0);
+          if (SWIGLU) {
+            tma_load_2d(sB + s * C::kStageB, &tm_w, &full[s], kb * BK, n0);
+            tma_load_2d(sB + s * C::kStageB + C::kStageB / 2, &tm_w, &full[s], kb * BK,
+                        p.N + n0);
+          } else {
+            tma_load_2d(sB + s * C::kStageB, &tm_w, &full[s], kb * BK, n0);
+          }
         } else {
-          tma_load_2d(sB + s * C::kStageB, &tm_w, &full[s], kb * BK, n0);
+          // {64, row, k-block} boxes: smem [k-block][row][128 B]; SwiGLU W as
+          // {64, row, half, k-block}: [k-block][gate rows | up rows][128 B]
+          tma_load_3d(sA + s * C::kStageA, &tm_x, &full[s], 0, m0, kb * KS);
+          if (SWIGLU)
+            tma_load_4d(sB + s * C::kStageB, &tm_w, &full[s], 0, n0, 0, kb * KS);
+          else
+            tma_load_3d(sB + s * C::kStageB, &tm_w, &full[s], 0, n0, kb * KS);
         }
       }
     }
@@ -146,14 +168,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(&full[s], (it / S) & 1, p.err, 2);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * kStageA);
+        const uint32_t a0 = smem_u32(sA + s * C::kStageA);
         const uint32_t b0 = smem_u32(sB + s * C::kStageB);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
+        for (int k = 0; k < KS * BK / 16; ++k) {
           // K-major, 128B swizzle: 8-row groups 1024 B apart; a K step of 16
-          // elements advances the start address by 32 bytes inside the row.
-          const uint64_t ad = make_sdesc(a0 + k * 32, 16, 1024, 2);
-          const uint64_t bd = make_sdesc(b0 + k * 32, 16, 1024, 2);
+          // elements advances the start address by 32 bytes inside the row;
+          // k-block j of the stage starts j sub-tiles further.
+          const uint32_t j = k >> 2, kk = k & 3;
+          const uint64_t ad = make_sdesc(a0 + j * kSubA + kk * 32, 16, 1024, 2);
+          const uint64_t bd = make_sdesc(b0 + j * C::kSubB + kk * 32, 16, 1024, 2);
           tc_mma_f16(acc, ad, bd, idesc, (kb | k) != 0);
         }
         tc_commit(&empty[s]);
@@ -273,19 +297,48 @@ int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const
               "tensor-core path needs 16-byte aligned x/W rows (K and ldx multiples of 8)");
   const bool sw = act == TPP_ACT_SWIGLU;
   const int64_t wrows = sw ? 2 * N : N;
+  // k-blocks per stage: 2 (one 3-D / 4-D box per operand and stage) when the
+  // rows are whole 64-element k-blocks, else 1 (2-D boxes, ragged K zero-filled)
+  static const bool ks2_on = [] {  // TPP_TC_KS=1 forces one k-block per stage (A/B)
+    const char* e = getenv("TPP_TC_KS");
+    return !(e && e[0] == '1');
+  }();
+  const int ks = (K % 64 == 0 && ks2_on) ? 2 : 1;
   CUtensorMap tx, tw;
-  {
-    uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
-    uint64_t strides[1] = {(uint64_t)ldx * 2};
-    uint32_t box[2] = {BK, BM};
-    int rc = make_tmap(&tx, x, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != TPP_OK) return rc;
-  }
-  {
+  if (ks == 1) {
+    {
+      uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+      uint64_t strides[1] = {(uint64_t)ldx * 2};
+      uint32_t box[2] = {BK, BM};
+      int rc = make_tmap(&tx, x, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != TPP_OK) return rc;
+    }
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)wrows};
     uint64_t strides[1] = {(uint64_t)K * 2};
-    uint32_t box[2] = {BK, (uint32_t)(sw ? TcCfg<true>::BN / 2 : TcCfg<false>::BN)};
+    uint32_t box[2] = {BK, (uint32_t)(sw ? TcCfg<true, 1>::BN / 2 : TcCfg<false, 1>::BN)};
     int rc = make_tmap(&tw, w, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != TPP_OK) return rc;
+  } else {
+    const uint64_t nkb = (uint64_t)(K / 64);
+    {
+      uint64_t dims[3] = {64, (uint64_t)M, nkb};
+      uint64_t strides[2] = {(uint64_t)ldx * 2, 128};
+      uint32_t box[3] = {64, BM, 2};
+      int rc = make_tmap(&tx, x, dtype, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc != TPP_OK) return rc;
+    }
+    int rc;
+    if (sw) {
+      uint64_t dims[4] = {64, (uint64_t)N, 2, nkb};
+      uint64_t strides[3] = {(uint64_t)K * 2, (uint64_t)N * K * 2, 128};
+      uint32_t box[4] = {64, (uint32_t)(TcCfg<true, 2>::BN / 2), 2, 2};
+      rc = make_tmap(&tw, w, dtype, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      uint64_t dims[3] = {64, (uint64_t)N, nkb};
+      uint64_t strides[2] = {(uint64_t)K * 2, 128};
+      uint32_t box[3] = {64, (uint32_t)TcCfg<false, 2>::BN, 2};
+      rc = make_tmap(&tw, w, dtype, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     if (rc != TPP_OK) return rc;
   }
   CUtensorMap ty;
@@ -304,19 +357,25 @@ int linear_tc(const void* x, int64_t ldx, const void* w, const void* bias, const
   a.M = (int)M; a.N = (int)N; a.K = (int)K; a.act = act;
   a.vec_ok = y_tma && (!residual || aligned16(residual));
   a.err = device_error_flag();
-  const int nout = sw ? TcCfg<true>::NOUT : TcCfg<false>::NOUT;
+  const int nout = ks == 2 ? (sw ? TcCfg<true, 2>::NOUT : TcCfg<false, 2>::NOUT)
+                           : (sw ? TcCfg<true, 1>::NOUT : TcCfg<false, 1>::NOUT);
   const int64_t tiles = ((N + nout - 1) / nout) * ((M + BM - 1) / BM);
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());  // persistent
-  const size_t smem = sw ? TcCfg<true>::kSmem : TcCfg<false>::kSmem;
   return TPP_DISPATCH_HALF(dtype, T, [&] {
-    auto kern = sw ? linear_tc_kernel<T, true> : linear_tc_kernel<T, false>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess) {
-      set_error("linear_tc_kernel: cannot reserve shared memory");
-      return (int)TPP_ERR_LAUNCH;
-    }
-    return launch("linear_tc_kernel", kern, dim3((unsigned)grid), dim3(kThreads), smem, st, 0,
-                  tx, tw, ty, a);
+    auto go = [&](auto kern, size_t smem) -> int {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess) {
+        set_error("linear_tc_kernel: cannot reserve shared memory");
+        return (int)TPP_ERR_LAUNCH;
+      }
+      return launch("linear_tc_kernel", kern, dim3((unsigned)grid), dim3(kThreads), smem, st, 0,
+                    tx, tw, ty, a);
+    };
+    if (ks == 2)
+      return sw ? go(linear_tc_kernel<T, true, 2>, TcCfg<true, 2>::kSmem)
+                : go(linear_tc_kernel<T, false, 2>, TcCfg<false, 2>::kSmem);
+    return sw ? go(linear_tc_kernel<T, true, 1>, TcCfg<true, 1>::kSmem)
+              : go(linear_tc_kernel<T, false, 1>, TcCfg<false, 1>::kSmem);
   });
 }
 
