@@ -56,6 +56,12 @@ const char* tpp_last_error(void);
 const char* tpp_version(void);
 /* Number of kernel launches this library has issued in the calling process. */
 uint64_t tpp_launch_count(void);
+/* SM budget for the launches the calling host thread makes next (0 = the
+ * whole device, the default): decode linears and decode attention size
+ * their grids for `sms` SMs.  Lets independent sub-batches recorded as
+ * parallel CUDA-graph branches each plan for their share of the GPU.  No
+ * reference counterpart. */
+int tpp_set_sm_budget(int sms);
 /* Reads and clears (synchronising `stream`) the current device's error flag,
  * which a kernel sets when one of its bounded device-side waits runs out
  * instead of spinning forever.  Returns 0 if no wait expired, the nonzero

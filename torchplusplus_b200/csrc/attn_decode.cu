@@ -29,7 +29,7 @@ int attn_decode_num_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t range) {
   const int64_t G = Hkv > 0 ? Hq / Hkv : 1;
   const int64_t passes = (G + 7) / 8;
   const int64_t ctas = B * Hkv * passes;
-  int64_t target = (8LL * num_sms() + ctas - 1) / (ctas > 0 ? ctas : 1);
+  int64_t target = (8LL * sm_budget() + ctas - 1) / (ctas > 0 ? ctas : 1);
   int64_t maxs = range / 128;
   if (maxs < 1) maxs = 1;
   if (target > maxs) target = maxs;

@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
 int decode_mma_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t range) {
   const int64_t G = Hq / Hkv;
   const int64_t ctas = B * Hkv * ((G + QR - 1) / QR);
-  int64_t s = (2LL * num_sms()) / (ctas > 0 ? ctas : 1);
+  int64_t s = (2LL * sm_budget()) / (ctas > 0 ? ctas : 1);
   int64_t maxs = (range + KT - 1) / KT;
   if (maxs < 1) maxs = 1;
   if (s > maxs) s = maxs;

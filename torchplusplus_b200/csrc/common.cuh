@@ -44,6 +44,12 @@ inline int num_sms() {
   return cached[dev];
 }
 
+// SMs a decode-step launch plans for: all of the device's unless the calling
+// host thread set a budget (tpp_set_sm_budget), so that independent
+// sub-batches recorded as parallel graph branches each size their grids for
+// their share of the GPU and run side by side.
+int sm_budget();
+
 // ---------------------------------------------------------------------------
 // Element types.
 // ---------------------------------------------------------------------------

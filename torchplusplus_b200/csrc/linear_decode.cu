@@ -504,7 +504,7 @@ int launch_skinny(const void* x, int64_t ldx, const void* w, SkinnyArgs& a, int 
     const int rc = make_tmap(&tx, x, dtype, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != TPP_OK) return rc;
   }
-  const int sms = num_sms();
+  const int sms = sm_budget();
   const int tiles = (a.N + NOUT - 1) / NOUT;
   const int nkb = (a.K + BK - 1) / BK;
   // Enough CTAs for two per SM; every split keeps >= 2 k-blocks.

@@ -845,7 +845,7 @@ int launch_xs8_wide(const void* x, int64_t ldx, const void* q, XsArgs& a, cudaSt
     return TPP_ERR_LAUNCH;
   }
   const int groups = (a.N + kWideNR - 1) / kWideNR;
-  const int grid = groups < num_sms() ? groups : num_sms();
+  const int grid = groups < sm_budget() ? groups : sm_budget();
   return launch("linear_xs8_wide_kernel", kern, dim3((unsigned)grid), dim3((kWideKW + 1) * 32),
                 smem, st, 1u, tx, a);
 }
@@ -987,7 +987,7 @@ bool xs_chunks(int bn, int nr, int nro, int nkb, size_t limit, size_t ring_limit
 // memory, or one per SM within 227 KB) and take a single-chunk plan with
 // the fewest operand bytes per CTA; otherwise the multi-chunk fallback.
 bool plan_xs(int64_t M, int64_t N, int64_t K, int act, XsLaunch& out, bool w8 = false) {
-  const int sms = num_sms();
+  const int sms = sm_budget();
   const int per_row = act == TPP_ACT_SWIGLU ? 2 : 1;
   const int nkb = (int)(K / 64);
   size_t best = ~(size_t)0;
@@ -1086,7 +1086,7 @@ extern "C" unsigned tpp_debug_xs_launches() { return g_xs_launch; }
 // Outputs per CTA (SwiGLU CTAs hold that many gate rows plus as many up
 // rows) for an N-wide layer on this device, or 0 when N is too wide.
 int xs_outputs_per_cta(int64_t N, int act) {
-  const int sms = num_sms();
+  const int sms = num_sms();  // fixed per device: packed weight images depend on it
   const int per_row = act == TPP_ACT_SWIGLU ? 2 : 1;  // weight rows per output
   int64_t nro = (N + sms - 1) / sms;
   nro = (nro + 7) / 8 * 8;

@@ -8,7 +8,13 @@ namespace tpp {
 static thread_local std::string g_last_error;
 static std::atomic<uint64_t> g_launches{0};
 
+static thread_local int g_sm_budget = 0;
+
 void set_error(const std::string& msg) { g_last_error = msg; }
+int sm_budget() {
+  const int n = num_sms();
+  return g_sm_budget > 0 && g_sm_budget < n ? g_sm_budget : n;
+}
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 bool pdl_enabled() {
@@ -34,3 +40,11 @@ int check_launch(const char* what) {
 extern "C" const char* tpp_last_error(void) { return tpp::g_last_error.c_str(); }
 extern "C" const char* tpp_version(void) { return "tpp_b200 0.1 (sm_100a)"; }
 extern "C" uint64_t tpp_launch_count(void) { return tpp::g_launches.load(); }
+extern "C" int tpp_set_sm_budget(int sms) {
+  if (sms < 0) {
+    tpp::set_error("tpp_set_sm_budget: sms must be >= 0 (0 = the whole device)");
+    return TPP_ERR_SHAPE;
+  }
+  tpp::g_sm_budget = sms;
+  return TPP_OK;
+}

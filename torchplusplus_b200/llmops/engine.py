@@ -142,6 +142,17 @@ class DecodeEngine:
 
     # ------------------------------------------------------------ one step
     def _step_lane(self, ln: dict, warm: Optional[torch.cuda.Stream] = None) -> None:
+        # several lanes run side by side as graph branches: each plans its
+        # grids for its share of the SMs
+        nl = len(self.lanes)
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        ops.set_sm_budget(sms // nl if nl > 1 else 0)
+        try:
+            self._step_lane_launches(ln, warm)
+        finally:
+            ops.set_sm_budget(0)
+
+    def _step_lane_launches(self, ln: dict, warm: Optional[torch.cuda.Stream]) -> None:
         n, Hq, Hkv, D = ln["n"], self.Hq, self.Hkv, self.D
         x = ln["x"]
         ops.embedding(ln["tokens"], self.emb, out=x)

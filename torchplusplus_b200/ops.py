@@ -350,6 +350,12 @@ def l2_prefetch(t: torch.Tensor) -> None:
     N.call("tpp_l2_prefetch", t.data_ptr(), n - n % 16, N.stream_of(t))
 
 
+def set_sm_budget(sms: int) -> None:
+    """Decode launches made next from this thread plan their grids for `sms`
+    SMs (0 = the whole device); see tpp_set_sm_budget."""
+    N.call("tpp_set_sm_budget", int(sms))
+
+
 def hgemv(weight: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """y[N] = weight[N,K] @ x[K] with fp32 accumulation."""
     _cuda(weight, x)
