@@ -1,0 +1,76 @@
+// Probe: the decode linear's MMA loop (32 tokens x 48 weight rows x K 1024,
+// 8 warps, operands resident in 128B-swizzled smem) in three schedules.
+#include <cstdio>
+#include <cuda_runtime.h>
+#include "../mma_common.cuh"
+using namespace tpp;
+using T = __nv_bfloat16;
+constexpr int MT = 2, NT = 6, NTM = 8, NKB = 16, BN = 32, NR = 48, KW = 8;
+
+template <int V>
+__global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint8_t* xs = sm;                       // [kb][BN][128]
+  uint8_t* ws = sm + NKB * BN * 128;      // [kb][NR][128]
+  for (int i = threadIdx.x; i < (NKB * (BN + NR) * 128) / 4; i += 256) ((uint32_t*)sm)[i] = 0x3c003c00u ^ i;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[MT][NTM][4] = {};
+  const uint32_t xb = (uint32_t)__cvta_generic_to_shared(xs), wb = (uint32_t)__cvta_generic_to_shared(ws);
+  auto offa = [&](int kk, int mi) { const int row = mi * 16 + (lane & 15); const int ch = kk * 2 + (lane >> 4); return (uint32_t)(row * 128 + ((ch ^ (row & 7)) << 4)); };
+  auto offb = [&](int kk, int np) { const int nt = (2 * np + 1 < NT) ? 2 * np + ((lane >> 4) & 1) : 2 * np; const int n = nt * 8 + (lane & 7); const int ch = kk * 2 + ((lane >> 3) & 1); return (uint32_t)(n * 128 + ((ch ^ (n & 7)) << 4)); };
+  __syncthreads();
+  long long t0 = clock64();
+  auto step = [&](int j, int kk) {
+    uint32_t a[MT][4], b[NTM / 2][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xb + j * BN * 128 + offa(kk, mi), a[mi]);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) ldsm_x4(wb + j * NR * 128 + offb(kk, np), b[np]);
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+        mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+      }
+  };
+  for (int rep = 0; rep < 8; ++rep) {
+    if (V == 0) {        // current: warp = (k16 step, k-block parity)
+      const int kk = warp & 3, jp = warp >> 2;
+      for (int j = jp; j < NKB; j += 2) step(j, kk);
+    } else if (V == 1) { // same, unrolled by 2
+      const int kk = warp & 3, jp = warp >> 2;
+#pragma unroll 2
+      for (int j = jp; j < NKB; j += 2) step(j, kk);
+    } else {             // warp = whole k-blocks w, w+8: all four k16 steps each
+#pragma unroll
+      for (int j = warp; j < NKB; j += KW)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) step(j, kk);
+    }
+  }
+  __syncthreads();
+  long long t1 = clock64();
+  float s = 0; for (int mi = 0; mi < MT; ++mi) for (int n = 0; n < NTM; ++n) for (int q = 0; q < 4; ++q) s += acc[mi][n][q];
+  sink[blockIdx.x * 256 + threadIdx.x] = s;
+  if (threadIdx.x == 0) out[blockIdx.x] = (t1 - t0) / 8;
+}
+
+int main() {
+  long long* d; float* sink; long long h[148];
+  cudaMalloc(&d, sizeof(h)); cudaMalloc(&sink, 148 * 256 * 4);
+  const int smem = NKB * (BN + NR) * 128;
+  for (int v = 0; v < 3; ++v) {
+    auto k = v == 0 ? probe<0> : v == 1 ? probe<1> : probe<2>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    for (int ctas : {1, 128}) {
+      k<<<ctas, 256, smem>>>(d, sink); cudaDeviceSynchronize();
+      k<<<ctas, 256, smem>>>(d, sink);
+      cudaError_t e = cudaDeviceSynchronize(); if (e) { printf("%s\n", cudaGetErrorString(e)); return 1; }
+      cudaMemcpy(h, d, sizeof(long long) * ctas, cudaMemcpyDeviceToHost);
+      long long mx = 0; for (int i = 0; i < ctas; ++i) mx = h[i] > mx ? h[i] : mx;
+      printf("variant %d ctas %3d: %lld clk per pass (%.0f FMA/clk/SM)\n", v, ctas, mx, 32.0 * 48 * 1024 / mx);
+    }
+  }
+}
