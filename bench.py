@@ -174,6 +174,7 @@ def run_reference(args, rank, world):
                                             "batch": args.batch, "prompt": PROMPT, "gen": GEN,
                                             "device": "host CPU"},
             "cpu_baseline": {k: b[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "value_scope": "the host CPU of the box: does not grow with n_gpus",
             "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
