@@ -175,11 +175,19 @@ def test_linear_decode_ragged_bias_residual(MNK):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("act", ["none", "silu", "gelu", "swiglu"])
-@pytest.mark.parametrize("MNK", [(2048, 3072, 1024), (65, 256, 64), (300, 1000, 200),
+@pytest.mark.parametrize("MNK", [(2048, 3072, 1024), (65, 256, 64), (300, 1000, 200), (200, 384, 128),
                                  (512, 2048, 3072)])
 def test_linear_tensor_core(dtype, act, MNK):
     M, N, K = MNK
     _linear_case(M, N, K, act, dtype)
+
+
+@pytest.mark.parametrize("MNK", [(300, 1000, 200), (200, 384, 128), (2048, 3072, 1024)])
+def test_linear_tensor_core_bias_residual(MNK):
+    """Bias + residual epilogue on the 256-row-tile path (and its ragged last
+    tile: one half partly or wholly past M)."""
+    M, N, K = MNK
+    _linear_case(M, N, K, "gelu", torch.bfloat16, bias=True, residual=True)
 
 
 def test_linear_tensor_core_bias_residual():
