@@ -8,7 +8,7 @@ using T = __nv_bfloat16;
 constexpr int MT = 2, NT = 6, NTM = 8, NKB = 16, BN = 32, NR = 48, KW = 8;
 
 template <int V>
-__global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink) {
+__global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink, int nt_rt) {
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* xs = sm;                       // [kb][BN][128]
   uint8_t* ws = sm + NKB * BN * 128;      // [kb][NR][128]
@@ -21,6 +21,81 @@ __global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink) {
   auto offb = [&](int kk, int np) { const int nt = (2 * np + 1 < NT) ? 2 * np + ((lane >> 4) & 1) : 2 * np; const int n = nt * 8 + (lane & 7); const int ch = kk * 2 + ((lane >> 3) & 1); return (uint32_t)(n * 128 + ((ch ^ (n & 7)) << 4)); };
   __syncthreads();
   long long t0 = clock64();
+  float ssl[MT][2] = {};
+  auto sq2 = [](uint32_t v) { float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v)); return f.x * f.x + f.y * f.y; };
+  auto step_rt = [&](int j, int kk) {   // runtime n-tile count and the RMSNorm sums, as built
+    uint32_t a[MT][4], b[NTM / 2][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xb + j * BN * 128 + offa(kk, mi), a[mi]);
+#pragma unroll
+    for (int np = 0; np < NTM / 2; ++np) { if (2 * np >= nt_rt) break; ldsm_x4(wb + j * NR * 128 + offb(kk, np), b[np]); }
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+      ssl[mi][0] += sq2(a[mi][0]) + sq2(a[mi][2]);
+      ssl[mi][1] += sq2(a[mi][1]) + sq2(a[mi][3]);
+#pragma unroll
+      for (int np = 0; np < NTM / 2; ++np) {
+        if (2 * np >= nt_rt) break;
+        mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+        if (2 * np + 1 < nt_rt) mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+      }
+    }
+  };
+  auto step_rt2 = [&](int j, int kk) {   // runtime n-tile count only
+    uint32_t a[MT][4], b[NTM / 2][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xb + j * BN * 128 + offa(kk, mi), a[mi]);
+#pragma unroll
+    for (int np = 0; np < NTM / 2; ++np) { if (2 * np >= nt_rt) break; ldsm_x4(wb + j * NR * 128 + offb(kk, np), b[np]); }
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int np = 0; np < NTM / 2; ++np) {
+        if (2 * np >= nt_rt) break;
+        mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+        if (2 * np + 1 < nt_rt) mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+      }
+  };
+  auto step_n = [&](int j, int kk) {     // static n-tiles + RMSNorm sums
+    uint32_t a[MT][4], b[NTM / 2][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xb + j * BN * 128 + offa(kk, mi), a[mi]);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) ldsm_x4(wb + j * NR * 128 + offb(kk, np), b[np]);
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+      ssl[mi][0] += sq2(a[mi][0]) + sq2(a[mi][2]);
+      ssl[mi][1] += sq2(a[mi][1]) + sq2(a[mi][3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+        mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+      }
+    }
+  };
+  unsigned long long ss2[MT][2] = {};
+  auto sqacc = [](unsigned long long& acc, uint32_t v) {
+    unsigned long long x;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(v << 16), "r"(v & 0xffff0000u));
+    asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(acc) : "l"(x));
+  };
+  auto step_p = [&](int j, int kk) {     // static n-tiles + packed-FMA RMSNorm sums
+    uint32_t a[MT][4], b[NTM / 2][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) ldsm_x4(xb + j * BN * 128 + offa(kk, mi), a[mi]);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) ldsm_x4(wb + j * NR * 128 + offb(kk, np), b[np]);
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) {
+      sqacc(ss2[mi][0], a[mi][0]); sqacc(ss2[mi][0], a[mi][2]);
+      sqacc(ss2[mi][1], a[mi][1]); sqacc(ss2[mi][1], a[mi][3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        mma<T>(acc[mi][2 * np], a[mi], b[np][0], b[np][1]);
+        mma<T>(acc[mi][2 * np + 1], a[mi], b[np][2], b[np][3]);
+      }
+    }
+  };
   auto step = [&](int j, int kk) {
     uint32_t a[MT][4], b[NTM / 2][4];
 #pragma unroll
@@ -43,6 +118,15 @@ __global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink) {
       const int kk = warp & 3, jp = warp >> 2;
 #pragma unroll 2
       for (int j = jp; j < NKB; j += 2) step(j, kk);
+    } else if (V == 6) {
+      const int kk = warp & 3, jp = warp >> 2;
+      for (int j = jp; j < NKB; j += 2) step_p(j, kk);
+    } else if (V == 4 || V == 5) {
+      const int kk = warp & 3, jp = warp >> 2;
+      for (int j = jp; j < NKB; j += 2) { if (V == 4) step_rt2(j, kk); else step_n(j, kk); }
+    } else if (V == 3) { // as built: runtime n-tiles + RMSNorm sums
+      const int kk = warp & 3, jp = warp >> 2;
+      for (int j = jp; j < NKB; j += 2) step_rt(j, kk);
     } else {             // warp = whole k-blocks w, w+8: all four k16 steps each
 #pragma unroll
       for (int j = warp; j < NKB; j += KW)
@@ -52,7 +136,7 @@ __global__ void __launch_bounds__(256, 1) probe(long long* out, float* sink) {
   }
   __syncthreads();
   long long t1 = clock64();
-  float s = 0; for (int mi = 0; mi < MT; ++mi) for (int n = 0; n < NTM; ++n) for (int q = 0; q < 4; ++q) s += acc[mi][n][q];
+  float s = ssl[0][0] + ssl[1][1] + (float)(ss2[0][0] ^ ss2[1][1]); for (int mi = 0; mi < MT; ++mi) for (int n = 0; n < NTM; ++n) for (int q = 0; q < 4; ++q) s += acc[mi][n][q];
   sink[blockIdx.x * 256 + threadIdx.x] = s;
   if (threadIdx.x == 0) out[blockIdx.x] = (t1 - t0) / 8;
 }
@@ -61,12 +145,12 @@ int main() {
   long long* d; float* sink; long long h[148];
   cudaMalloc(&d, sizeof(h)); cudaMalloc(&sink, 148 * 256 * 4);
   const int smem = NKB * (BN + NR) * 128;
-  for (int v = 0; v < 3; ++v) {
-    auto k = v == 0 ? probe<0> : v == 1 ? probe<1> : probe<2>;
+  for (int v = 0; v < 7; ++v) {
+    auto k = v == 0 ? probe<0> : v == 1 ? probe<1> : v == 2 ? probe<2> : v == 3 ? probe<3> : v == 4 ? probe<4> : v == 5 ? probe<5> : probe<6>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     for (int ctas : {1, 128}) {
-      k<<<ctas, 256, smem>>>(d, sink); cudaDeviceSynchronize();
-      k<<<ctas, 256, smem>>>(d, sink);
+      k<<<ctas, 256, smem>>>(d, sink, NT); cudaDeviceSynchronize();
+      k<<<ctas, 256, smem>>>(d, sink, NT);
       cudaError_t e = cudaDeviceSynchronize(); if (e) { printf("%s\n", cudaGetErrorString(e)); return 1; }
       cudaMemcpy(h, d, sizeof(long long) * ctas, cudaMemcpyDeviceToHost);
       long long mx = 0; for (int i = 0; i < ctas; ++i) mx = h[i] > mx ? h[i] : mx;
