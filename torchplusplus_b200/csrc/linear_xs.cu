@@ -1078,14 +1078,11 @@ int xs_dispatch_nt(const void* x, int64_t ldx, const void* w, XsArgs& a, int dty
             : launch_xs<T, 32, NTM, false, NORM, W8, NTC>(x, ldx, w, a, dtype, st, L);
 }
 
-// bf16/fp16 weights: the exact n-tile count as a template constant (see
-// linear_xs_kernel); fp8 weights keep the runtime count.
+// The exact n-tile count as a template constant (see linear_xs_kernel).
 template <typename T, int NTM, bool NORM, bool W8>
 int xs_dispatch_exact(const void* x, int64_t ldx, const void* w, XsArgs& a, int dtype,
                       cudaStream_t st, const XsLaunch& L, int nt) {
-  if constexpr (W8) {
-    return xs_dispatch_nt<T, NTM, NORM, W8>(x, ldx, w, a, dtype, st, L);
-  } else {
+  {
     if constexpr (NTM == 2) {
       return nt == 1 ? xs_dispatch_nt<T, 2, NORM, W8, 1>(x, ldx, w, a, dtype, st, L)
                      : xs_dispatch_nt<T, 2, NORM, W8, 2>(x, ldx, w, a, dtype, st, L);
