@@ -389,6 +389,55 @@ int tpp_decode_advance(const int64_t* next_tokens, int64_t* out_ids, int64_t ld_
                        int64_t out_cap, int32_t* positions, int32_t* seqlens, int64_t B,
                        void* stream);
 
+/* ---- persistent single-sequence decode step ------------------------------- */
+/* One decoder layer's operands for tpp_decode_step_persistent (device
+ * pointers; the array of these lives in device memory).  Weights are
+ * [out, in] row-major in the step's dtype, with the RMSNorm weight in front
+ * of a projection folded into it (w[r, k] * gamma[k]): wqkv [(Hq+2Hkv)*D, E]
+ * (q rows, k rows, v rows), wo [E, Hq*D], wgu [2F, E] (gate rows, then up
+ * rows), wdown [E, F]; qn / kn the per-head q / k RMSNorm weights [D] (may
+ * be NULL); kc / vc the layer's cache [Hkv, Smax, D] (one sequence). */
+typedef struct {
+  const void* wqkv;
+  const void* qn;
+  const void* kn;
+  const void* wo;
+  const void* wgu;
+  const void* wdown;
+  void* kc;
+  void* vc;
+} tpp_decode_layer;
+
+/* Bytes of device workspace tpp_decode_step_persistent needs (zero it once
+ * before the first step), or 0 when the model shape is outside its plan. */
+int64_t tpp_decode_step_persistent_workspace(int64_t E, int64_t Hq, int64_t Hkv, int64_t D,
+                                             int64_t F, int64_t Smax);
+
+/* The whole greedy decode step of one sequence in ONE cooperative launch of
+ * one CTA per SM: embedding of tokens[0] -> per layer [RMSNorm + QKV ->
+ * q/k RMSNorm + RoPE at positions[0] + K/V append + attention over keys
+ * 0..positions[0] (split over CTAs, merged by every CTA that needs it) ->
+ * o-proj + residual -> RMSNorm + gate/up + SwiGLU -> down + residual] ->
+ * final RMSNorm + LM head (lm_head = W_head * final-norm weight, logits
+ * written, [V] in dtype) -> argmax -> tokens[0] = next, out_ids[p+1] = next
+ * (if p+1 < out_cap), positions[0] = p+1, seqlens[0] = p+2.  The phases are
+ * separated by grid-wide barriers (bounded waits; an expiry raises the
+ * device error flag and the kernel returns) instead of kernel boundaries,
+ * and each CTA's producer warp streams the weight slices of the coming
+ * phases into shared memory across the barriers.  cos/sin: fp16 RoPE tables
+ * [ctx, D] (row stride cs_stride); dtype bf16 or fp16.  Replaces the
+ * reference's per-token loop of torchpp/llmops/llm.py:263-282 over
+ * examples/LLM/fastqwen3.py:99-118 at batch 1.  Returns TPP_ERR_UNSUPPORTED
+ * for shapes outside its plan (a phase's weight slice must fit 96 KB). */
+int tpp_decode_step_persistent(const tpp_decode_layer* layers, int64_t n_layers,
+                               const void* emb, const void* lm_head, const void* cos,
+                               const void* sin, int64_t cs_stride, int64_t* tokens,
+                               int32_t* positions, int32_t* seqlens, int64_t* out_ids,
+                               int64_t out_cap, void* logits, void* workspace,
+                               int64_t workspace_bytes, int64_t E, int64_t Hq, int64_t Hkv,
+                               int64_t D, int64_t F, int64_t V, int64_t Smax, float eps,
+                               int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,10 @@ SIGNATURES: dict[str, tuple] = {
     "tpp_launch_count": (C.c_uint64, []),
     "tpp_device_error": (_i32, [_p]),
     "tpp_set_sm_budget": (_i32, [_i32]),
+    "tpp_decode_step_persistent_workspace": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64]),
+    "tpp_decode_step_persistent": (_i32, [_p, _i64, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _i64,
+                                          _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                          _i64, _f32, _i32, _p]),
     "tpp_debug_expire_wait": (_i32, [C.c_uint32, _i32, _p]),
     "tpp_rmsnorm": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i64, _f32, _i32, _p]),
     "tpp_add_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _f32, _i32, _p]),

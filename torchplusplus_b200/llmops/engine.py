@@ -18,6 +18,7 @@ cache per step (kvcache.py:106-107) and synchronises on token.item()
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional
 
 import torch
@@ -35,7 +36,7 @@ class DecodeEngine:
     (see the measurement noted below)."""
 
     def __init__(self, model, batch_size: int, max_seq_len: int, lanes: int | None = None,
-                 weight_format: str = "native"):
+                 weight_format: str = "native", persistent: bool | None = None):
         cfg = model.cfg
         dev = model.out_head.weight.device
         self.model = model
@@ -134,6 +135,24 @@ class DecodeEngine:
             if max(ln["n"] for ln in self.lanes) > 32:
                 raise ValueError("fp8 decode weights serve lanes of at most 32 sequences")
             self.lm_head_f8 = ops.Fp8Weight(self.lm_head_f)
+        # batch 1, native weights, on request (persistent=True or
+        # TPP_PERSISTENT=1): the whole step as one persistent cooperative
+        # kernel (tpp_decode_step_persistent).  Off by default: measured
+        # 961 tok/s against 1155 for the launch-per-phase graph at batch 1.
+        self.persistent = None
+        if persistent is None:
+            persistent = os.environ.get("TPP_PERSISTENT", "0") == "1"
+        if persistent and B == 1 and weight_format == "native" and \
+                self.cos.dtype == torch.float16:
+            try:
+                self.persistent = ops.PersistentDecode(
+                    [dict(wqkv=L["wqkv_f"], qn=L["qn"], kn=L["kn"], wo=L["wo"], wgu=L["wgu_f"],
+                          wdown=L["wdown"], kc=c.k_cache[0], vc=c.v_cache[0])
+                     for L, c in zip(self.layers, self.caches)],
+                    self.emb, self.lm_head_f, self.cos, self.sin, self.Hq, self.Hkv, self.D,
+                    max_seq_len, self.eps)
+            except ValueError:
+                self.persistent = None
         if weight_format == "fp8":
             for L in self.layers:
                 L["f8"] = dict(qkv=ops.Fp8Weight(L["wqkv_f"]), o=ops.Fp8Weight(L["wo"]),
@@ -142,6 +161,10 @@ class DecodeEngine:
 
     # ------------------------------------------------------------ one step
     def _step_lane(self, ln: dict, warm: Optional[torch.cuda.Stream] = None) -> None:
+        if self.persistent is not None and self.sampling is None:
+            self.persistent.step(self.tokens, self.positions, self.seqlens, self.out_ids[0],
+                                 self.logits[0])
+            return
         # several lanes run side by side as graph branches: each plans its
         # grids for its share of the SMs
         nl = len(self.lanes)

@@ -143,10 +143,12 @@ class Qwen3(LLMInference):
         projections on e4m3 weights); None keeps self.decode_weight_format."""
         from .engine import DecodeEngine
         fmt = weight_format or getattr(self, "decode_weight_format", "native")
+        pers = getattr(self, "decode_persistent", None)
         e = self._engine
         if e is None or e.batch_size != batch_size or e.max_seq_len < max_seq_len or \
-                e.weight_format != fmt:
-            self._engine = e = DecodeEngine(self, batch_size, max_seq_len, weight_format=fmt)
+                e.weight_format != fmt or (pers is not None and (e.persistent is not None) != pers):
+            self._engine = e = DecodeEngine(self, batch_size, max_seq_len, weight_format=fmt,
+                                            persistent=pers)
         return e
 
     @torch.inference_mode()

@@ -350,6 +350,55 @@ def l2_prefetch(t: torch.Tensor) -> None:
     N.call("tpp_l2_prefetch", t.data_ptr(), n - n % 16, N.stream_of(t))
 
 
+class PersistentDecode:
+    """Operands of tpp_decode_step_persistent for one sequence: the per-layer
+    pointer table (tpp_decode_layer records, in device memory) and the
+    zero-initialised workspace.  `layers` holds per layer the folded QKV
+    weight, q/k norm weights, o-proj weight, folded gate/up weight, down
+    weight and the layer's [Hkv, Smax, D] K and V caches."""
+
+    def __init__(self, layers: list, emb: torch.Tensor, lm_head_folded: torch.Tensor,
+                 cos: torch.Tensor, sin: torch.Tensor, Hq: int, Hkv: int, D: int, Smax: int,
+                 eps: float = 1e-6):
+        _cuda(emb, lm_head_folded, cos, sin)
+        self.dt = _half(emb, "embedding")
+        if cos.dtype != torch.float16 or sin.dtype != torch.float16 or cos.shape[1] != D:
+            raise ValueError("RoPE tables must be fp16 [ctx, D]")
+        dev = emb.device
+        self.keep = [emb, lm_head_folded, cos, sin]
+        ptrs = []
+        for L in layers:
+            for t in (L["wqkv"], L["qn"], L["kn"], L["wo"], L["wgu"], L["wdown"], L["kc"], L["vc"]):
+                if t is not None:
+                    _same_dtype(emb, t)
+                    if not t.is_contiguous():
+                        raise ValueError("persistent decode operands must be contiguous")
+                    self.keep.append(t)
+                ptrs.append(0 if t is None else t.data_ptr())
+        self.table = torch.tensor(ptrs, dtype=torch.int64).to(dev)
+        self.n_layers = len(layers)
+        self.E = emb.shape[1]
+        self.V = lm_head_folded.shape[0]
+        self.F = layers[0]["wgu"].shape[0] // 2
+        self.Hq, self.Hkv, self.D, self.Smax, self.eps = Hq, Hkv, D, Smax, eps
+        nbytes = int(N.lib().tpp_decode_step_persistent_workspace(self.E, Hq, Hkv, D, self.F, Smax))
+        if nbytes <= 0:
+            raise ValueError("model shape outside the persistent decode plan")
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.emb, self.lm_head, self.cos, self.sin = emb, lm_head_folded, cos, sin
+
+    def step(self, tokens: torch.Tensor, positions: torch.Tensor, seqlens: torch.Tensor | None,
+             out_ids: torch.Tensor | None, logits: torch.Tensor) -> None:
+        """One greedy decode step (see tpp_decode_step_persistent)."""
+        N.call("tpp_decode_step_persistent", self.table.data_ptr(), self.n_layers,
+               self.emb.data_ptr(), self.lm_head.data_ptr(), self.cos.data_ptr(),
+               self.sin.data_ptr(), self.cos.stride(0), tokens.data_ptr(), positions.data_ptr(),
+               N.ptr(seqlens), N.ptr(out_ids), 0 if out_ids is None else out_ids.shape[-1],
+               logits.data_ptr(), self.ws.data_ptr(), self.ws.numel(), self.E, self.Hq,
+               self.Hkv, self.D, self.F, self.V, self.Smax, float(self.eps), self.dt,
+               N.stream_of(logits))
+
+
 def set_sm_budget(sms: int) -> None:
     """Decode launches made next from this thread plan their grids for `sms`
     SMs (0 = the whole device); see tpp_set_sm_budget."""
