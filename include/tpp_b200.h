@@ -396,7 +396,9 @@ int tpp_decode_advance(const int64_t* next_tokens, int64_t* out_ids, int64_t ld_
  * of a projection folded into it (w[r, k] * gamma[k]): wqkv [(Hq+2Hkv)*D, E]
  * (q rows, k rows, v rows), wo [E, Hq*D], wgu [2F, E] (gate rows, then up
  * rows), wdown [E, F]; qn / kn the per-head q / k RMSNorm weights [D] (may
- * be NULL); kc / vc the layer's cache [Hkv, Smax, D] (one sequence). */
+ * be NULL); kc / vc the layer's cache [Hkv, Smax, D] (one sequence).  Every
+ * pointer 16-byte aligned: the kernel bulk-copies weight slices, cached K/V
+ * rows and the norm weights into shared memory. */
 typedef struct {
   const void* wqkv;
   const void* qn;
@@ -424,7 +426,8 @@ int64_t tpp_decode_step_persistent_workspace(int64_t E, int64_t Hq, int64_t Hkv,
  * separated by grid-wide barriers (bounded waits; an expiry raises the
  * device error flag and the kernel returns) instead of kernel boundaries,
  * and each CTA's producer warp streams the weight slices of the coming
- * phases into shared memory across the barriers.  cos/sin: fp16 RoPE tables
+ * phases (paced: TPP_DP_PACE="<KiB>,<in flight>", default "8,6") and its
+ * attention unit's cached K/V rows into shared memory across the barriers.  cos/sin: fp16 RoPE tables
  * [ctx, D] (row stride cs_stride); dtype bf16 or fp16.  Replaces the
  * reference's per-token loop of torchpp/llmops/llm.py:263-282 over
  * examples/LLM/fastqwen3.py:99-118 at batch 1.  Returns TPP_ERR_UNSUPPORTED

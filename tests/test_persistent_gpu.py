@@ -13,9 +13,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _model(dtype=torch.bfloat16, seed=0, layers=2):
-    cfg = Qwen3Config(vocab_size=1000, context_length=512, embed_dim=512, n_heads=4,
-                      n_layers=layers, head_dim=128, n_kv_heads=2, hidden_dim=1024, dtype=dtype)
+def _model(dtype=torch.bfloat16, seed=0, layers=2, heads=(4, 2)):
+    cfg = Qwen3Config(vocab_size=1000, context_length=512, embed_dim=512, n_heads=heads[0],
+                      n_layers=layers, head_dim=128, n_kv_heads=heads[1], hidden_dim=1024,
+                      dtype=dtype)
     m = Qwen3(cfg, device=DEV).init_weights(0.05, seed=seed)
     with torch.no_grad():
         for n, p in m.named_parameters():
@@ -24,10 +25,11 @@ def _model(dtype=torch.bfloat16, seed=0, layers=2):
     return m
 
 
+@pytest.mark.parametrize("heads", [(4, 2), (8, 2), (2, 2)], ids=["gq2", "gq4", "gq1"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("prompt", [1, 37, 200])
-def test_persistent_step_matches_graph_step(dtype, prompt):
-    m = _model(dtype)
+def test_persistent_step_matches_graph_step(dtype, prompt, heads):
+    m = _model(dtype, heads=heads)
     ids = torch.randint(0, 1000, (1, prompt), generator=torch.Generator().manual_seed(prompt))
     with torch.inference_mode():
         ea = DecodeEngine(m, 1, 256, persistent=True)
@@ -74,4 +76,29 @@ def test_persistent_generate_graph_replays():
     picked = logits.gather(-1, out[:, 30:].to(DEV)[..., None])[..., 0]
     best = logits.max(-1).values
     assert bool((picked >= best - 5e-2 * best.abs().clamp(min=1.0)).all())
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("prompt", [600, 2600])
+def test_persistent_step_at_qwen3_widths(prompt):
+    """Qwen3-0.6B layer widths (E 1024, 16/8 heads, F 3072): at 600 keys
+    every attention unit's cached rows are staged in shared memory behind its
+    o-proj slice; at 2600 a unit's range (145 keys) outgrows that room (135
+    rows on 148 SMs) and its last rows come from the cache directly."""
+    cfg = Qwen3Config(vocab_size=4096, context_length=4096, n_layers=2, dtype=torch.bfloat16)
+    m = Qwen3(cfg, device=DEV).init_weights(0.02, seed=5)
+    ids = torch.randint(0, 4096, (1, prompt), generator=torch.Generator().manual_seed(prompt))
+    with torch.inference_mode():
+        ea = DecodeEngine(m, 1, 3072, persistent=True)
+        eb = DecodeEngine(m, 1, 3072, persistent=False)
+        assert ea.persistent is not None
+        ea.prefill(ids)
+        eb.prefill(ids)
+        for step in range(3):
+            eb.tokens.copy_(ea.tokens)
+            eb.out_ids.copy_(ea.out_ids)
+            ea.step_eager()
+            eb.step_eager()
+            la, lb = ea.logits.float(), eb.logits.float()
+            assert (la - lb).abs().max().item() <= 2e-2 * max(1.0, lb.abs().max().item()), step
     assert ops.device_error() == 0

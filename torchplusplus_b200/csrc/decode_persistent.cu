@@ -23,6 +23,7 @@
 // GEMVs run on CUDA cores (one token: one weight byte is used once), a warp
 // per output row, fp32 accumulation; every stored activation is rounded to
 // the step's dtype as the launch-per-phase path rounds it.
+#include <stdio.h>
 #include <stdlib.h>
 #include "tc_common.cuh"
 
@@ -36,6 +37,13 @@ constexpr uint32_t kSlot = 96 * 1024;    // one weight slot
 constexpr int kMaxG = 4;                 // query heads per kv head (at most)
 constexpr int kTK = 256;                 // keys per attention tile
 constexpr int kMaxCTAs = 256;
+constexpr int kPaceMax = 8;
+constexpr int kMaxRes = 64;              // residual rows per CTA (at most)
+#ifdef TPP_DP_NR1
+constexpr int kRG = 1;
+#else
+constexpr int kRG = 4;                   // rows of a warp dotted together
+#endif              // paced weight chunks in flight (at most)
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 #ifdef TPP_DEBUG_STAMPS
@@ -107,6 +115,8 @@ struct StepArgs {
   int E, Hq, Hkv, D, F, V, Smax;
   float eps, scale_log2;
   int lm_rows_per_job;  // LM-head rows per weight job
+  int pace_chunk;       // layer weight slices stream in chunks of this many bytes ...
+  int pace_depth;       // ... with at most this many in flight per CTA (0: one burst)
   int* err;
 };
 
@@ -131,8 +141,9 @@ __device__ __forceinline__ void grid_arrive(const Ws& w, unsigned long long& tar
   cons_sync();
   if (threadIdx.x == 0) {
     target += gridDim.x;
-    __threadfence();
-    atomicAdd(reinterpret_cast<unsigned long long*>(w.count), 1ull);
+    // release at gpu scope: covers this CTA's writes ordered before it by
+    // the CTA barrier above
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(w.count) : "memory");
   }
 }
 __device__ bool grid_wait(const Ws& w, unsigned long long target, int* flag, int* err,
@@ -182,25 +193,52 @@ __device__ __forceinline__ void load_vec(float* xs, const void* src, int n, int 
   }
 }
 
-// Row r of a [rows][K] slice in shared memory dotted with xs[K] (fp32),
-// by one warp; returns the full sum in every lane.
-template <typename T>
-__device__ __forceinline__ float row_dot(const uint8_t* slot, int r, int K, const float* xs,
-                                         int lane) {
-  const T* w = reinterpret_cast<const T*>(slot) + (size_t)r * K;
-  float acc = 0.f;
+// Up to NR rows (local indices rr[0..nr)) of a [rows][K] slice in shared
+// memory dotted with xs[K] by one warp, all NR accumulations in flight at
+// once (one pass over xs); with SS also sum(xs^2) (every warp covers all of
+// K, so each gets the whole sum without a block reduction).  Full sums in
+// every lane.
+template <typename T, int NR, bool SS>
+__device__ __forceinline__ void rows_dot(const uint8_t* slot, const int (&rr)[NR], int nr, int K,
+                                         const float* xs, int lane, float (&out)[NR],
+                                         float& ss) {
+  float acc[NR];
+  const T* wr[NR];
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    acc[i] = 0.f;
+    wr[i] = reinterpret_cast<const T*>(slot) + (size_t)(i < nr ? rr[i] : rr[0]) * K;
+  }
+  float s2 = 0.f;
   for (int k = lane * 8; k < K; k += 256) {
-    const uint4 v = *reinterpret_cast<const uint4*>(w + k);
-    float f[8];
-    unpack8<T>(v, f);
     const float4 a = *reinterpret_cast<const float4*>(xs + k);
     const float4 b = *reinterpret_cast<const float4*>(xs + k + 4);
-    acc = fmaf(f[0], a.x, acc); acc = fmaf(f[1], a.y, acc);
-    acc = fmaf(f[2], a.z, acc); acc = fmaf(f[3], a.w, acc);
-    acc = fmaf(f[4], b.x, acc); acc = fmaf(f[5], b.y, acc);
-    acc = fmaf(f[6], b.z, acc); acc = fmaf(f[7], b.w, acc);
+    if (SS) {
+      s2 = fmaf(a.x, a.x, s2); s2 = fmaf(a.y, a.y, s2); s2 = fmaf(a.z, a.z, s2);
+      s2 = fmaf(a.w, a.w, s2); s2 = fmaf(b.x, b.x, s2); s2 = fmaf(b.y, b.y, s2);
+      s2 = fmaf(b.z, b.z, s2); s2 = fmaf(b.w, b.w, s2);
+    }
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      if (i >= nr) break;
+      float f[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(wr[i] + k), f);
+      float v = acc[i];
+      v = fmaf(f[0], a.x, v); v = fmaf(f[1], a.y, v); v = fmaf(f[2], a.z, v);
+      v = fmaf(f[3], a.w, v); v = fmaf(f[4], b.x, v); v = fmaf(f[5], b.y, v);
+      v = fmaf(f[6], b.z, v); v = fmaf(f[7], b.w, v);
+      acc[i] = v;
+    }
   }
-  return warp_sum(acc);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < NR; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    if (SS) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+#pragma unroll
+  for (int i = 0; i < NR; ++i) out[i] = acc[i];
+  ss = s2;
 }
 
 // Contiguous share [r0, r1) of `rows` for CTA c of G.
@@ -273,18 +311,58 @@ __device__ __forceinline__ int n_jobs(const StepArgs& a, int c, int G) {
 }
 
 
+// The attention unit of CTA c: kv head h, key range [k0, k1) of the Lk = pos
+// + 1 keys (S units per head, >= ~64 keys each).  The cached keys are
+// [k0, kend); the unit that owns position pos also takes the new key.
+struct AttUnit {
+  bool in_att, own_new;
+  int h, sp, S, k0, kend, ktot;
+  int nst;  // cached keys staged in shared memory (after the o-proj weights)
+};
+__device__ __forceinline__ AttUnit att_unit(const StepArgs& a, int pos, int c, int G,
+                                            uint32_t o_bytes) {
+  AttUnit u;
+  const int Lk = pos + 1;
+  u.S = max(1, min((Lk + 63) / 64, G / a.Hkv));
+  u.in_att = c < a.Hkv * u.S;
+  u.h = u.in_att ? c / u.S : 0;
+  u.sp = u.in_att ? c % u.S : 0;
+  const int per = (Lk + u.S - 1) / u.S;
+  u.k0 = u.sp * per;
+  const int k1 = min(Lk, u.k0 + per);
+  u.own_new = u.in_att && pos >= u.k0 && pos < k1;
+  u.kend = u.own_new ? pos : k1;
+  u.ktot = u.in_att ? max(0, u.kend - u.k0) + (u.own_new ? 1 : 0) : 0;
+  // K rows, V rows (256 B each) and the two norm weight rows after the
+  // o-proj slice in its slot
+  const int room = ((int)kSlot - (int)o_bytes - 512) / 512;
+  u.nst = u.in_att ? max(0, min(u.kend - u.k0, room)) : 0;
+  return u;
+}
+
 // Shared memory (after the two 1024-aligned weight slots).
 struct Smem {
-  float xs[3072 + 64];        // the phase's input vector (fp32), >= max(E, Hq D, F)
-  float q[kMaxG][128];        // attention: normed + rotated q rows
-  float knew[128], vnew[128];
-  float sc[kMaxG][kTK];       // scores / probabilities of one key tile
+  union {
+    struct {
+      float xs[3072 + 64];    // the phase's input vector (fp32), >= max(E, Hq D, F)
+      float q[kMaxG][128];    // attention: normed + rotated q rows
+      float knew[128], vnew[128];
+      float sc[kMaxG][kTK];   // scores / probabilities of one key tile
+    };
+    float wpart[kCons / 32][2][128];  // attention end (<= 2 query heads): each warp's P.V sums
+  };
   float oacc[kMaxG][128];     // the unit's P.V sums (warps added)
   float mrun[kMaxG], lrun[kMaxG], corr[kMaxG];
   float red[32];
+  float xres[kMaxRes];        // this CTA's rows of the residual stream (o-proj / down rows)
   float best_v[16];
   int best_i[16];
   uint64_t full[2], empty[2];
+  uint64_t pace[kPaceMax];
+  uint64_t kvbar;             // the layer's staged K/V rows + norm weights landed
+  float cs[2][128];           // cos, sin rows of this step's position
+  int kv_issued;              // layers whose K/V staging the producer issued
+  int kvfail;                 // a staged-K/V wait gave up
   int flag;
   int abort_local;            // consumers gave up: the producer stops
   int issued;                 // jobs the producer issued
@@ -324,6 +402,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
+    for (int i = 0; i < kPaceMax; ++i) mbar_init(&sm.pace[i], 1);
+    mbar_init(&sm.kvbar, 1);
+    sm.kv_issued = 0;
+    sm.kvfail = 0;
     sm.abort_local = 0;
     sm.issued = 0;
     fence_mbar_init();
@@ -332,9 +414,48 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
 
   if (warp == kProdWarp) {
     // ---------------- producer: weight slices of every phase, in order ----------------
+    // A layer's slices are needed one phase at a time, but a slot frees up
+    // while latency-bound phases (attention, barriers) run: issued as one
+    // burst per CTA, a slice fills the memory queues for microseconds and
+    // every dependent load of those phases waits behind it.  So layer slices
+    // stream in pace_chunk pieces with at most pace_depth in flight per CTA
+    // (their own mbarriers), and the slot's full barrier is arrived on once
+    // the slice has landed.  LM-head chunks have nothing behind them and go
+    // out as single bursts.
     if (lane == 0) {
+      const int depth = a.pace_depth;
+      uint32_t q = 0;  // paced chunks issued
+      bool alive = true;
+      auto pace_wait = [&](uint32_t k, bool stop_on_abort) {  // chunk k has landed
+        for (uint32_t i = 0; i < kSpinLimit; ++i) {
+          if (mbar_try_wait(&sm.pace[k % depth], (k / depth) & 1)) return true;
+          if (stop_on_abort && *(volatile int*)&sm.abort_local) break;
+        }
+        return false;
+      };
+      // with an o-proj slice (its slot sits idle through QKV and attention):
+      // this CTA's cached K/V rows of the layer's attention unit and the q/k
+      // norm weights, after the weights (they depend on nothing in the
+      // step), on their own barrier
+      const int ppos = a.positions[0];
+      const AttUnit pu = att_unit(a, ppos, c, G, job_of(a, 1, c, G).bytes0);
+      int kv_issued = 0;
+      auto stage_kv = [&](int j, uint8_t* dst) {
+        if (!pu.in_att || j >= 4 * a.n_layers || (j & 3) != 1) return;
+        const tpp_decode_layer& L = a.layers[j >> 2];
+        const uint32_t rb = (uint32_t)pu.nst * 256u;
+        mbar_arrive_expect_tx(&sm.kvbar, 2 * rb + (L.qn ? 256u : 0u) + (L.kn ? 256u : 0u));
+        const int64_t row0 = ((int64_t)pu.h * a.Smax + pu.k0) * 128;
+        if (rb) {
+          bulk_load(dst, static_cast<const T*>(L.kc) + row0, rb, &sm.kvbar);
+          bulk_load(dst + rb, static_cast<const T*>(L.vc) + row0, rb, &sm.kvbar);
+        }
+        if (L.qn) bulk_load(dst + 2 * rb, L.qn, 256u, &sm.kvbar);
+        if (L.kn) bulk_load(dst + 2 * rb + 256, L.kn, 256u, &sm.kvbar);
+        *(volatile int*)&sm.kv_issued = ++kv_issued;
+      };
       int j = 0;
-      for (; j < njobs; ++j) {
+      for (; j < njobs && alive; ++j) {
         const int s = j & 1;
         if (j >= 2) {
           bool got = false;
@@ -345,11 +466,35 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           if (!got) break;
         }
         const Job jb = job_of(a, j, c, G);
-        mbar_arrive_expect_tx(&sm.full[s], jb.bytes0 + jb.bytes1);
-        if (jb.bytes0) bulk_load(slot[s], jb.src0, jb.bytes0, &sm.full[s]);
-        if (jb.bytes1) bulk_load(slot[s] + jb.bytes0, jb.src1, jb.bytes1, &sm.full[s]);
+        if (depth == 0 || j >= 4 * a.n_layers) {
+          mbar_arrive_expect_tx(&sm.full[s], jb.bytes0 + jb.bytes1);
+          if (jb.bytes0) bulk_load(slot[s], jb.src0, jb.bytes0, &sm.full[s]);
+          if (jb.bytes1) bulk_load(slot[s] + jb.bytes0, jb.src1, jb.bytes1, &sm.full[s]);
+          stage_kv(j, slot[s] + jb.bytes0 + jb.bytes1);
+          continue;
+        }
+        for (int part = 0; part < 2 && alive; ++part) {
+          const uint8_t* src = part ? jb.src1 : jb.src0;
+          const uint32_t bytes = part ? jb.bytes1 : jb.bytes0;
+          uint8_t* dst = slot[s] + (part ? jb.bytes0 : 0u);
+          for (uint32_t off = 0; off < bytes; off += (uint32_t)a.pace_chunk) {
+            if (q >= (uint32_t)depth && !pace_wait(q - depth, true)) { alive = false; break; }
+            const uint32_t n = min((uint32_t)a.pace_chunk, bytes - off);
+            mbar_arrive_expect_tx(&sm.pace[q % depth], n);
+            bulk_load(dst + off, src + off, n, &sm.pace[q % depth]);
+            ++q;
+          }
+        }
+        if (alive) stage_kv(j, slot[s] + jb.bytes0 + jb.bytes1);
+        // the slice has landed once its last depth chunks have
+        for (uint32_t k = q > (uint32_t)depth ? q - depth : 0u; k < q && alive; ++k)
+          if (!pace_wait(k, true)) alive = false;
+        if (!alive) break;
+        mbar_arrive(&sm.full[s]);
       }
-      *(volatile int*)&sm.issued = j;
+      // chunks in flight land before the CTA can exit
+      for (uint32_t k = q > (uint32_t)depth ? q - depth : 0u; k < q; ++k) pace_wait(k, false);
+      *(volatile int*)&sm.issued = j;  // jobs whose full barrier completes
     }
     __syncwarp();
   } else {
@@ -383,6 +528,12 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     constexpr int GQ = NG;  // query heads per kv head
     const float inv_e = 1.f / (float)a.E;
     const void* emb_row = static_cast<const T*>(a.emb) + tok * a.E;
+    const uint32_t o_bytes = job_of(a, 1, c, G).bytes0;
+    const AttUnit au = att_unit(a, pos, c, G, o_bytes);
+    int kv_waited = 0;
+    for (int i = ctid; i < 256; i += kCons)
+      sm.cs[i >> 7][i & 127] =
+          __half2float((i < 128 ? a.cosp : a.sinp)[(int64_t)pos * a.cs_stride + (i & 127)]);
     int r0, r1;
     for (int l = 0; l < a.n_layers && ok; ++l) {
       const tpp_decode_layer& L = a.layers[l];
@@ -393,64 +544,65 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         DP_TS(8 + l * 16 + 0);
         load_vec<T>(sm.xs, xsrc, a.E, ctid);
         cons_sync();
-        const float rs = rsqrtf(block_sumsq<T>(sm, a.E, ctid) * inv_e + a.eps);
+        DP_TS(8 + l * 16 + 14);
+        {  // this CTA's residual rows, for the o-proj and down phases
+          int e0, e1;
+          share(a.E, c, G, e0, e1);
+          for (int i = ctid; i < e1 - e0; i += kCons) sm.xres[i] = sm.xs[e0 + i];
+        }
         share(R, c, G, r0, r1);
-        for (int r = r0 + warp; r < r1 && ok; r += kCons / 32) {
-          const float v = row_dot<T>(sl, r - r0, a.E, sm.xs, lane);
-          if (lane == 0) static_cast<T*>(w.qkv)[r] = from_f32<T>(v * rs);
+        // warp w: rows r0 + w + 15 i, four at a time
+#ifdef TPP_DP_REP
+        for (int rep = 0; rep < TPP_DP_REP; ++rep)
+#endif
+        for (int rb = r0 + warp; rb < r1 && ok; rb += kRG * (kCons / 32)) {
+          int rr[kRG];
+#pragma unroll
+          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
+          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
+          float v[kRG], ss;
+          rows_dot<T, kRG, true>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
+          const float rs = rsqrtf(ss * inv_e + a.eps);
+          if (lane < nr) {
+            float vi = v[0];
+#pragma unroll
+            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
+            static_cast<T*>(w.qkv)[rb + lane * (kCons / 32)] = from_f32<T>(vi * rs);
+          }
         }
         DP_TS(8 + l * 16 + 1);
         release();
       }
       if (!ok) break;
       grid_arrive(w, bar_target);
-      // ---- the attention unit of this CTA (kv head h, key range sp) is known
-      // before the QKV results: its first cached K/V rows and the q/k
-      // prologue's constants load under the barrier ----
       constexpr int NW = kCons / 32;
-      const int Lk = pos + 1;
-      const int S = max(1, min((Lk + 63) / 64, G / a.Hkv));
-      const int units = a.Hkv * S;
-      const bool in_att = c < units;
-      const int h = in_att ? c / S : 0, sp = in_att ? c % S : 0;
-      const int per = (Lk + S - 1) / S;
-      const int k0 = sp * per, k1 = min(Lk, k0 + per);
-      const bool own_new = in_att && pos >= k0 && pos < k1;
-      const int kend = own_new ? pos : k1;  // cached keys; the new one comes last
-      const int ktot = in_att ? max(0, kend - k0) + (own_new ? 1 : 0) : 0;
+      const int S = au.S, h = au.h, sp = au.sp, k0 = au.k0, kend = au.kend, ktot = au.ktot;
+      const int nst = au.nst;
+      const bool in_att = au.in_att, own_new = au.own_new;
       const T* kc = static_cast<const T*>(L.kc) + (int64_t)h * a.Smax * 128;
       const T* vc = static_cast<const T*>(L.vc) + (int64_t)h * a.Smax * 128;
-      uint2 kpre[4], vpre[4];
-      float nwv[4] = {1.f, 1.f, 1.f, 1.f}, cv4[4] = {0.f, 0.f, 0.f, 0.f}, sv4[4] = {0.f, 0.f, 0.f, 0.f};
-      bool has_nw = false;
-      if (in_att) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int key = k0 + warp + u * NW;
-          kpre[u] = make_uint2(0, 0);
-          vpre[u] = make_uint2(0, 0);
-          if (key < kend) {
-            kpre[u] = *reinterpret_cast<const uint2*>(kc + (int64_t)key * 128 + lane * 4);
-            vpre[u] = *reinterpret_cast<const uint2*>(vc + (int64_t)key * 128 + lane * 4);
-          }
-        }
-        if (warp <= GQ) {
-          const T* nw = static_cast<const T*>(warp < GQ ? L.qn : L.kn);
-          has_nw = nw != nullptr;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (has_nw) nwv[j] = to_f32(nw[lane * 4 + j]);
-            cv4[j] = __half2float(a.cosp[(int64_t)pos * a.cs_stride + lane * 4 + j]);
-            sv4[j] = __half2float(a.sinp[(int64_t)pos * a.cs_stride + lane * 4 + j]);
-          }
-        }
-      }
+      // staged rows: K [nst][128], V [nst][128], q-norm, k-norm weights
+      const T* kvs = reinterpret_cast<const T*>(slot[(4 * l + 1) & 1] + o_bytes);
       if (!grid_wait(w, bar_target, &sm.flag, a.err, 62)) { ok = false; break; }
       DP_TS(8 + l * 16 + 2);
       // ---- attention ----
       {
         if (in_att) {
           const int D = 128;
+          if (!mbar_wait(&sm.kvbar, l & 1, a.err, 69)) sm.kvfail = 1;
+          kv_waited = l + 1;
+          float nwv[4] = {1.f, 1.f, 1.f, 1.f}, cv4[4], sv4[4];
+          bool has_nw = false;
+          if (warp <= GQ) {
+            has_nw = (warp < GQ ? L.qn : L.kn) != nullptr;
+            const T* nw = kvs + 2 * nst * 128 + (warp < GQ ? 0 : 128);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (has_nw) nwv[j] = to_f32(nw[lane * 4 + j]);
+              cv4[j] = sm.cs[0][lane * 4 + j];
+              sv4[j] = sm.cs[1][lane * 4 + j];
+            }
+          }
           // q rows of the G query heads, the new k row (normed + rotated) and v row
           if (warp <= GQ + 1) {
             const T* qkv = static_cast<const T*>(w.qkv);
@@ -462,6 +614,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
 #pragma unroll
               for (int j = 0; j < 4; ++j) x[j] = to_f32(e[j]);
             }
+            if (l < 2) DP_TS(476 + l * 10);
             if (warp <= GQ) {
               if (has_nw) {
                 float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
@@ -491,9 +644,15 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
               for (int j = 0; j < 4; ++j) dst[j] = from_f32<T>(x[j]);
             }
           }
+          if (l < 2) DP_TS(477 + l * 10);
           if (ctid < GQ) { sm.mrun[ctid] = -INFINITY; sm.lrun[ctid] = 0.f; }
           for (int i = ctid; i < kMaxG * 128; i += kCons) (&sm.oacc[0][0])[i] = 0.f;
           cons_sync();
+          const bool kv_ok = sm.kvfail == 0;
+          if (!kv_ok) {
+            ok = false;
+            if (ctid == 0) atomicExch(w.abortf, 1u);
+          }
           if (l < 2) DP_TS(470 + l * 10);
           // Warp w takes keys w, w + 15, ... of each tile; lane l holds head
           // dims [4l, 4l + 4) of q, k and v, so a key costs one coalesced
@@ -508,19 +667,25 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           for (int g = 0; g < NG; ++g)
 #pragma unroll
             for (int j = 0; j < 4; ++j) ow[g][j] = 0.f;
-          auto row4 = [&](const T* base, int key, float* f) {
-            if (key < kend) {
-              const uint2 u = *reinterpret_cast<const uint2*>(base + (int64_t)key * 128 + lane * 4);
+          // row `key` of K (which 0) or V (1): staged in shared memory, else
+          // from the cache, else (the new key) the prologue's row
+          auto row4 = [&](int which, int key, float* f) {
+            const int kk = key - k0;
+            if (kk < nst || key < kend) {
+              const uint2 u =
+                  kk < nst ? *reinterpret_cast<const uint2*>(kvs + (which * nst + kk) * 128 + lane * 4)
+                           : *reinterpret_cast<const uint2*>((which ? vc : kc) + (int64_t)key * 128 +
+                                                             lane * 4);
               const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
               for (int j = 0; j < 4; ++j) f[j] = to_f32(e[j]);
             } else {
-              const float* src = base == kc ? sm.knew : sm.vnew;
+              const float* src = which ? sm.vnew : sm.knew;
 #pragma unroll
               for (int j = 0; j < 4; ++j) f[j] = src[lane * 4 + j];
             }
           };
-          for (int t0 = 0; t0 < ktot; t0 += kTK) {
+          for (int t0 = 0; kv_ok && t0 < ktot; t0 += kTK) {
             const int nt = min(kTK, ktot - t0);
             // scores, 4 keys of a warp in flight at a time
             for (int i0 = warp; i0 < nt; i0 += 4 * NW) {
@@ -529,13 +694,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
               for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * NW;
                 if (i >= nt) continue;
-                if (t0 == 0 && i0 == warp && k0 + i < kend) {
-                  const T* e = reinterpret_cast<const T*>(&kpre[u]);
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) kf[u][j] = to_f32(e[j]);
-                } else {
-                  row4(kc, k0 + t0 + i, kf[u]);
-                }
+                row4(0, k0 + t0 + i, kf[u]);
               }
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
@@ -587,13 +746,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
               for (int u = 0; u < 4; ++u) {
                 const int i = i0 + u * NW;
                 if (i >= nt) continue;
-                if (t0 == 0 && i0 == warp && k0 + i < kend) {
-                  const T* e = reinterpret_cast<const T*>(&vpre[u]);
-#pragma unroll
-                  for (int j = 0; j < 4; ++j) vf[u][j] = to_f32(e[j]);
-                } else {
-                  row4(vc, k0 + t0 + i, vf[u]);
-                }
+                row4(1, k0 + t0 + i, vf[u]);
               }
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
@@ -611,73 +764,97 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
             cons_sync();
             if (l < 2 && t0 == 0) DP_TS(473 + l * 10);
           }
-          // sum the warps' o accumulators
-#pragma unroll
-          for (int g = 0; g < NG; ++g) {
-            if (g >= GQ) break;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) atomicAdd(&sm.oacc[g][lane * 4 + j], ow[g][j]);
-          }
-          cons_sync();
-          // partial (o, m, l) of each query head of this unit
+          // sum the warps' o accumulators: with <= 2 query heads each warp
+          // stores its sums (over the now idle vector / score buffers) and a
+          // thread per (head, dim) adds the 15; else shared-memory atomics
           const int npair = GQ * 128;
-          for (int pi = ctid; pi < npair; pi += kCons) {
-            const int g = pi / 128, d = pi % 128;
-            float* dst = w.part + ((int64_t)(h * GQ + g) * S + sp) * (128 + 2);
-            dst[d] = sm.oacc[g][d];
-            if (d == 0) { dst[128] = sm.mrun[g]; dst[129] = sm.lrun[g]; }
-          }
-          __threadfence();
-          cons_sync();
-          if (l < 2) DP_TS(474 + l * 10);
-          // the last unit of head h to finish merges its S partials: (m, l)
-          // staged once, per-head weights, then one (query head, dim) pair
-          // per thread with its S loads in flight
-          if (ctid == 0) {
-            const uint32_t prev = atomicAdd(&w.head_cnt[h], 1u);
-            const bool last = prev == (uint32_t)(S - 1);
-            if (last) atomicExch(&w.head_cnt[h], 0u);
-            sm.flag = last ? 1 : 0;
-          }
-          cons_sync();
-          if (sm.flag) {
-            __threadfence();
-            float* st = &sm.sc[0][0];  // [GQ][S] m -> weights, [GQ][S] l, [GQ] 1 / den
-            const int GS = GQ * S;
-            for (int i = ctid; i < GS; i += kCons) {
-              const float* src = w.part + ((int64_t)h * GQ * S + i) * 130;
-              st[i] = __ldcg(src + 128);
-              st[GS + i] = __ldcg(src + 129);
-            }
+          if constexpr (NG <= 2) {
+#pragma unroll
+            for (int g = 0; g < NG; ++g)
+              *reinterpret_cast<float4*>(&sm.wpart[warp][g][lane * 4]) =
+                  make_float4(ow[g][0], ow[g][1], ow[g][2], ow[g][3]);
             cons_sync();
-            if (ctid < GQ) {
-              float M = -INFINITY;
-              for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, st[ctid * S + s2]);
-              float den = 0.f;
-              for (int s2 = 0; s2 < S; ++s2) {
-                const float m2 = st[ctid * S + s2];
-                const float e = m2 == -INFINITY ? 0.f : exp2f(m2 - M);
-                st[ctid * S + s2] = e;
-                den = fmaf(e, st[GS + ctid * S + s2], den);
-              }
-              st[2 * GS + ctid] = den > 0.f ? 1.f / den : 0.f;
-            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < NG; ++g)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) atomicAdd(&sm.oacc[g][lane * 4 + j], ow[g][j]);
             cons_sync();
+          }
+          if (kv_ok) {
+            // partial (o, m, l) of each query head of this unit
             for (int pi = ctid; pi < npair; pi += kCons) {
               const int g = pi / 128, d = pi % 128;
-              const float* src = w.part + (int64_t)(h * GQ + g) * S * 130 + d;
-              float num = 0.f;
-#pragma unroll 8
-              for (int s2 = 0; s2 < S; ++s2) num = fmaf(st[g * S + s2], __ldcg(src + s2 * 130), num);
-              static_cast<T*>(w.o)[(int64_t)(h * GQ + g) * 128 + d] =
-                  from_f32<T>(num * st[2 * GS + g]);
+              float t;
+              if constexpr (NG <= 2) {
+                t = 0.f;
+#pragma unroll
+                for (int w2 = 0; w2 < kCons / 32; ++w2) t += sm.wpart[w2][g][d];
+              } else {
+                t = sm.oacc[g][d];
+              }
+              float* dst = w.part + ((int64_t)(h * GQ + g) * S + sp) * (128 + 2);
+              dst[d] = t;
+              if (d == 0) { dst[128] = sm.mrun[g]; dst[129] = sm.lrun[g]; }
+            }
+            cons_sync();
+            if (l < 2) DP_TS(474 + l * 10);
+            // the last unit of head h to finish merges its S partials.  The
+            // counter add is acq_rel at gpu scope: it releases this unit's
+            // partial (ordered before it by the CTA barrier) and, in the last
+            // unit, acquires every other unit's.
+            if (ctid == 0) {
+              uint32_t prev;
+              asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                           : "=r"(prev) : "l"(w.head_cnt + h) : "memory");
+              const bool last = prev == (uint32_t)(S - 1);
+              if (last) atomicExch(&w.head_cnt[h], 0u);
+              sm.flag = last ? 1 : 0;
+            }
+            cons_sync();
+            if (sm.flag) {
+              // one (query head, dim) pair per thread; the S partials' (o, m,
+              // l) are loaded 8 at a time with every load of a group in flight
+              // and folded with a running max
+              for (int pi = ctid; pi < npair; pi += kCons) {
+                const int g = pi / 128, d = pi % 128;
+                const float* src = w.part + (int64_t)(h * GQ + g) * S * 130;
+                float M = -INFINITY, den = 0.f, num = 0.f;
+                for (int s0 = 0; s0 < S; s0 += 8) {
+                  float mv[8], lv[8], ov[8];
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) {
+                    const bool in = s0 + u < S;
+                    const float* sp2 = src + (int64_t)(s0 + u) * 130;
+                    mv[u] = in ? __ldcg(sp2 + 128) : -INFINITY;
+                    lv[u] = in ? __ldcg(sp2 + 129) : 0.f;
+                    ov[u] = in ? __ldcg(sp2 + d) : 0.f;
+                  }
+                  float mc = M;
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) mc = fmaxf(mc, mv[u]);
+                  if (mc == -INFINITY) continue;
+                  const float cr = M == -INFINITY ? 0.f : exp2f(M - mc);
+                  den *= cr;
+                  num *= cr;
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) {
+                    const float e = mv[u] == -INFINITY ? 0.f : exp2f(mv[u] - mc);
+                    den = fmaf(e, lv[u], den);
+                    num = fmaf(e, ov[u], num);
+                  }
+                  M = mc;
+                }
+                static_cast<T*>(w.o)[(int64_t)(h * GQ + g) * 128 + d] =
+                    from_f32<T>(den > 0.f ? num / den : 0.f);
+              }
             }
           }
           if (l < 2) DP_TS(475 + l * 10);
         }
       }
       DP_TS(8 + l * 16 + 3);
-      if (!grid_sync(w, bar_target, &sm.flag, a.err, 63)) { ok = false; break; }
+      if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 63)) { ok = false; break; }
       DP_TS(8 + l * 16 + 4);
       // ---- o-proj + residual: x[r] = x[r] + o . Wo[r] ----
       {
@@ -686,10 +863,24 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         const int K = a.Hq * a.D;
         load_vec<T>(sm.xs, w.o, K, ctid);
         cons_sync();
+        DP_TS(8 + l * 16 + 15);
         share(a.E, c, G, r0, r1);
-        for (int r = r0 + warp; r < r1; r += kCons / 32) {
-          const float v = row_dot<T>(sl, r - r0, K, sm.xs, lane);
-          if (lane == 0) static_cast<T*>(w.x)[r] = from_f32<T>(ldT<T>(xsrc, r) + v);
+        for (int rb = r0 + warp; rb < r1; rb += kRG * (kCons / 32)) {
+          int rr[kRG];
+#pragma unroll
+          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
+          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
+          float v[kRG], ss;
+          rows_dot<T, kRG, false>(sl, rr, nr, K, sm.xs, lane, v, ss);
+          if (lane < nr) {
+            float vi = v[0];
+#pragma unroll
+            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
+            const int lr = rr[0] + lane * (kCons / 32);
+            const T nv = from_f32<T>(sm.xres[lr] + vi);
+            static_cast<T*>(w.x)[r0 + lr] = nv;
+            sm.xres[lr] = to_f32(nv);
+          }
         }
         release();
       }
@@ -701,13 +892,35 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         const uint8_t* sl = acquire();
         load_vec<T>(sm.xs, w.x, a.E, ctid);
         cons_sync();
-        const float rs = rsqrtf(block_sumsq<T>(sm, a.E, ctid) * inv_e + a.eps);
+        DP_TS(8 + l * 16 + 8);
         share(a.F, c, G, r0, r1);
         const int nf = r1 - r0;
-        for (int f = warp; f < nf; f += kCons / 32) {
-          const float g = row_dot<T>(sl, f, a.E, sm.xs, lane) * rs;
-          const float u = row_dot<T>(sl, nf + f, a.E, sm.xs, lane) * rs;
-          if (lane == 0) static_cast<T*>(w.ff)[r0 + f] = from_f32<T>(act_silu(g) * u);
+        // warp w: features w + 15 i, kGF at a time (gate and up rows each)
+        constexpr int kGF = kRG >= 2 ? kRG / 2 : 1;
+#ifdef TPP_DP_REP
+        for (int rep = 0; rep < TPP_DP_REP; ++rep)
+#endif
+        for (int fb = warp; fb < nf; fb += kGF * (kCons / 32)) {
+          int rr[2 * kGF];
+#pragma unroll
+          for (int i = 0; i < kGF; ++i) {
+            rr[2 * i] = fb + i * (kCons / 32);
+            rr[2 * i + 1] = nf + fb + i * (kCons / 32);
+          }
+          const int nr = 2 * min(kGF, (nf - fb + kCons / 32 - 1) / (kCons / 32));
+          float v[2 * kGF], ss;
+          rows_dot<T, 2 * kGF, true>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
+          const float rs = rsqrtf(ss * inv_e + a.eps);
+          if (lane < nr / 2) {
+            float g = v[0], u = v[1];
+#pragma unroll
+            for (int i = 1; i < kGF; ++i) {
+              g = lane == i ? v[2 * i] : g;
+              u = lane == i ? v[2 * i + 1] : u;
+            }
+            static_cast<T*>(w.ff)[r0 + fb + lane * (kCons / 32)] =
+                from_f32<T>(act_silu(g * rs) * (u * rs));
+          }
         }
         release();
       }
@@ -719,10 +932,24 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         const uint8_t* sl = acquire();
         load_vec<T>(sm.xs, w.ff, a.F, ctid);
         cons_sync();
+        DP_TS(8 + l * 16 + 11);
         share(a.E, c, G, r0, r1);
-        for (int r = r0 + warp; r < r1; r += kCons / 32) {
-          const float v = row_dot<T>(sl, r - r0, a.F, sm.xs, lane);
-          if (lane == 0) static_cast<T*>(w.x)[r] = from_f32<T>(ldT<T>(w.x, r) + v);
+        for (int rb = r0 + warp; rb < r1; rb += kRG * (kCons / 32)) {
+          int rr[kRG];
+#pragma unroll
+          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
+          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
+          float v[kRG], ss;
+          rows_dot<T, kRG, false>(sl, rr, nr, a.F, sm.xs, lane, v, ss);
+          if (lane < nr) {
+            float vi = v[0];
+#pragma unroll
+            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
+            const int lr = rr[0] + lane * (kCons / 32);
+            const T nv = from_f32<T>(sm.xres[lr] + vi);
+            static_cast<T*>(w.x)[r0 + lr] = nv;
+            sm.xres[lr] = to_f32(nv);
+          }
         }
         release();
       }
@@ -742,11 +969,22 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       for (int q = 0; jc < njobs && ok; ++q) {
         const uint8_t* sl = acquire();
         const int rr0 = v0 + q * a.lm_rows_per_job, rr1 = min(v1, rr0 + a.lm_rows_per_job);
-        for (int r = rr0 + warp; r < rr1; r += kCons / 32) {
-          const float v = rndT<T>(row_dot<T>(sl, r - rr0, a.E, sm.xs, lane) * rs);
+        for (int rb = rr0 + warp; rb < rr1; rb += kRG * (kCons / 32)) {
+          int rr[kRG];
+#pragma unroll
+          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - rr0;
+          const int nr = min(kRG, (rr1 - rb + kCons / 32 - 1) / (kCons / 32));
+          float v[kRG], ss;
+          rows_dot<T, kRG, false>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
           if (lane == 0) {
-            static_cast<T*>(a.logits)[r] = from_f32<T>(v);
-            if (v > bv || (v == bv && r < bi)) { bv = v; bi = r; }
+#pragma unroll
+            for (int i = 0; i < kRG; ++i) {
+              if (i >= nr) break;
+              const int r = rb + i * (kCons / 32);
+              const float vi = rndT<T>(v[i] * rs);
+              static_cast<T*>(a.logits)[r] = from_f32<T>(vi);
+              if (vi > bv || (vi == bv && r < bi)) { bv = vi; bi = r; }
+            }
           }
         }
         release();
@@ -792,12 +1030,14 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     // jobs issued but not consumed (an aborted step) land before the CTA exits
     __syncwarp();
     cons_sync();
-    if (ctid == 0) sm.red[0] = __int_as_float(jc);
+    if (ctid == 0) { sm.red[0] = __int_as_float(jc); sm.red[1] = __int_as_float(kv_waited); }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     const int consumed = __float_as_int(sm.red[0]);
     for (int j = consumed; j < sm.issued; ++j) mbar_wait(&sm.full[j & 1], (j >> 1) & 1, a.err, 68);
+    for (int k = __float_as_int(sm.red[1]); k < sm.kv_issued; ++k)
+      mbar_wait(&sm.kvbar, k & 1, a.err, 68);
   }
 }
 }  // namespace
@@ -825,7 +1065,7 @@ bool persistent_fits(int64_t E, int64_t Hq, int64_t Hkv, int64_t D, int64_t F) {
   return D == 128 && (GQ == 1 || GQ == 2 || GQ == 4) && GQ + 2 <= kCons / 32 && GQ * D <= 2 * kCons && Hkv <= 64 &&
          E % 8 == 0 && F % 8 == 0 && E <= 3072 && Hq * D <= 3072 && F <= 3072 &&
          per(R) * E * 2 <= kSlot && per(E) * Hq * D * 2 <= kSlot && 2 * per(F) * E * 2 <= kSlot &&
-         per(E) * F * 2 <= kSlot;
+         per(E) * F * 2 <= kSlot && per(E) <= kMaxRes;
 }
 }  // namespace
 
@@ -865,6 +1105,16 @@ extern "C" int tpp_decode_step_persistent(
   a.Smax = (int)Smax; a.eps = eps;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   a.lm_rows_per_job = (int)(kSlot / (E * 2));
+  // TPP_DP_PACE="<chunk KiB>,<chunks in flight>" (",0": one burst per slice)
+  a.pace_chunk = 8 * 1024;
+  a.pace_depth = 6;
+  if (const char* pe = getenv("TPP_DP_PACE")) {
+    int kb = 0, d = 0;
+    if (sscanf(pe, "%d,%d", &kb, &d) == 2 && kb >= 1 && kb <= 96 && d >= 0 && d <= kPaceMax) {
+      a.pace_chunk = kb * 1024;
+      a.pace_depth = d;
+    }
+  }
   a.err = device_error_flag();
   const size_t smem = 1024 + 2 * (size_t)kSlot + sizeof(Smem);
   cudaStream_t st = as_stream(stream);

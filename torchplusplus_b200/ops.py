@@ -371,8 +371,9 @@ class PersistentDecode:
             for t in (L["wqkv"], L["qn"], L["kn"], L["wo"], L["wgu"], L["wdown"], L["kc"], L["vc"]):
                 if t is not None:
                     _same_dtype(emb, t)
-                    if not t.is_contiguous():
-                        raise ValueError("persistent decode operands must be contiguous")
+                    if not t.is_contiguous() or t.data_ptr() % 16:
+                        raise ValueError("persistent decode operands must be contiguous and "
+                                         "16-byte aligned (they are bulk-copied)")
                     self.keep.append(t)
                 ptrs.append(0 if t is None else t.data_ptr())
         self.table = torch.tensor(ptrs, dtype=torch.int64).to(dev)
