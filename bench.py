@@ -669,18 +669,28 @@ def run_ours(args, rank, world, local):
                 "step_linear_time_us": rl["seconds"] * 1e6}
     extra = {}
     if rank == 0 and not args.skip_b1:
-        e1 = model.engine(1, cap)
-        e1.prefill(prompts[0][:1])
-        e1.capture()
-        e1.decode(8)
-        e1.prefill(prompts[0][:1])  # back to the prompt: nrep steps fill the capacity
-        torch.cuda.synchronize()
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record()
-        e1.decode(nrep)
-        a1.record()
-        a1.synchronize()
-        extra["batch1_decode_tokens_per_s"] = nrep / (a0.elapsed_time(a1) / 1e3)
+        # batch 1: the persistent one-kernel step (the default at batch 1)
+        # and the launch-per-phase graph beside it
+        for key, pers in (("batch1_decode_tokens_per_s", None),
+                          ("batch1_launch_graph_decode_tokens_per_s", False)):
+            model._engine = None
+            model.decode_persistent = pers
+            e1 = model.engine(1, cap)
+            e1.prefill(prompts[0][:1])
+            e1.capture()
+            e1.decode(8)
+            e1.prefill(prompts[0][:1])  # back to the prompt: nrep steps fill the capacity
+            torch.cuda.synchronize()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            e1.decode(nrep)
+            a1.record()
+            a1.synchronize()
+            extra[key] = nrep / (a0.elapsed_time(a1) / 1e3)
+            if pers is None:
+                extra["batch1_persistent_step"] = e1.persistent is not None
+            del e1
+        model.decode_persistent = None
         model._engine = None
     if rank == 0 and not args.skip_fp8:
         # the same decode with fp8 (e4m3, per-row scale) copies of the

@@ -67,11 +67,30 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 
 // Unpack 8 packed 16-bit elements (a uint4) into fp32.
+// Two packed 16-bit elements (low half first) of a 32-bit word into fp32,
+// with register operations only (taking the address of a register vector
+// can put it in local memory).
+template <typename T> struct Unpack2;
+template <> struct Unpack2<__half> {
+  static __device__ __forceinline__ void run(uint32_t w, float& lo, float& hi) {
+    unsigned short a, b;
+    asm("mov.b32 {%0, %1}, %2;" : "=h"(a), "=h"(b) : "r"(w));
+    lo = __half2float(__ushort_as_half(a));
+    hi = __half2float(__ushort_as_half(b));
+  }
+};
+template <> struct Unpack2<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(uint32_t w, float& lo, float& hi) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  }
+};
 template <typename T>
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = to_f32(e[i]);
+  Unpack2<T>::run(u.x, f[0], f[1]);
+  Unpack2<T>::run(u.y, f[2], f[3]);
+  Unpack2<T>::run(u.z, f[4], f[5]);
+  Unpack2<T>::run(u.w, f[6], f[7]);
 }
 template <typename T>
 __device__ __forceinline__ uint4 pack8(const float* f) {

@@ -39,11 +39,9 @@ constexpr int kTK = 256;                 // keys per attention tile
 constexpr int kMaxCTAs = 256;
 constexpr int kPaceMax = 8;
 constexpr int kMaxRes = 64;              // residual rows per CTA (at most)
-#ifdef TPP_DP_NR1
-constexpr int kRG = 1;
-#else
-constexpr int kRG = 4;                   // rows of a warp dotted together
-#endif              // paced weight chunks in flight (at most)
+constexpr int kRG = 4;                   // rows of one GEMV work item
+constexpr int kKC = 256;                 // K elements of one GEMV work item (8 a lane)
+constexpr int kMaxPart = 512;            // GEMV partial sums per phase (chunks x rows)
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 #ifdef TPP_DEBUG_STAMPS
@@ -181,64 +179,98 @@ __device__ __forceinline__ float ldT(const void* p, int64_t i) {
 template <typename T>
 __device__ __forceinline__ float rndT(float v) { return to_f32(from_f32<T>(v)); }
 
-// xs[0..n) = src[0..n) (dtype -> fp32), 8 elements (16 bytes) per load
+// xs[0..n) = src[0..n) (dtype -> fp32), 8 elements (16 bytes) per load.
+// With red != nullptr each warp also leaves its share of sum(x^2) in
+// red[warp] (read back with sumsq_of after the next consumer barrier).
 template <typename T>
-__device__ __forceinline__ void load_vec(float* xs, const void* src, int n, int ctid) {
+__device__ __forceinline__ void load_vec(float* xs, const void* src, int n, int ctid,
+                                         float* red = nullptr) {
   const uint4* p = static_cast<const uint4*>(src);
+  float ss = 0.f;
   for (int i = ctid; i < n / 8; i += kCons) {
     float f[8];
     unpack8<T>(__ldcg(p + i), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
     *reinterpret_cast<float4*>(xs + 8 * i) = make_float4(f[0], f[1], f[2], f[3]);
     *reinterpret_cast<float4*>(xs + 8 * i + 4) = make_float4(f[4], f[5], f[6], f[7]);
   }
+  if (red != nullptr) {
+    ss = warp_sum(ss);
+    if ((ctid & 31) == 0) red[ctid >> 5] = ss;
+  }
+}
+__device__ __forceinline__ float sumsq_of(const float* red) {
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCons / 32; ++w) t += red[w];
+  return t;
 }
 
-// Up to NR rows (local indices rr[0..nr)) of a [rows][K] slice in shared
-// memory dotted with xs[K] by one warp, all NR accumulations in flight at
-// once (one pass over xs); with SS also sum(xs^2) (every warp covers all of
-// K, so each gets the whole sum without a block reduction).  Full sums in
-// every lane.
-template <typename T, int NR, bool SS>
-__device__ __forceinline__ void rows_dot(const uint8_t* slot, const int (&rr)[NR], int nr, int K,
-                                         const float* xs, int lane, float (&out)[NR],
-                                         float& ss) {
-  float acc[NR];
-  const T* wr[NR];
-#pragma unroll
-  for (int i = 0; i < NR; ++i) {
-    acc[i] = 0.f;
-    wr[i] = reinterpret_cast<const T*>(slot) + (size_t)(i < nr ? rr[i] : rr[0]) * K;
-  }
-  float s2 = 0.f;
-  for (int k = lane * 8; k < K; k += 256) {
-    const float4 a = *reinterpret_cast<const float4*>(xs + k);
-    const float4 b = *reinterpret_cast<const float4*>(xs + k + 4);
-    if (SS) {
-      s2 = fmaf(a.x, a.x, s2); s2 = fmaf(a.y, a.y, s2); s2 = fmaf(a.z, a.z, s2);
-      s2 = fmaf(a.w, a.w, s2); s2 = fmaf(b.x, b.x, s2); s2 = fmaf(b.y, b.y, s2);
-      s2 = fmaf(b.z, b.z, s2); s2 = fmaf(b.w, b.w, s2);
+// Partial GEMV of this CTA's weight slice: rows [0, R) of a [R][K] slice in
+// shared memory (row stride K elements) dotted with x (fp32, shared).  The
+// work is cut into items of one 256-wide K chunk c x kRG rows; a consumer
+// warp takes items w, w + 15, ...; lane l holds x[256c + 8l, +8) in
+// registers, so x is read from shared memory once per item (not once per
+// row) and every weight byte once.  The kRG row sums are reduced across the
+// warp with a transposing butterfly (6 shuffles for 4 rows) and lane 8i
+// writes part[c * R + row i].  Callers sum the K/256 chunk partials of a row
+// in chunk order after a consumer barrier.
+template <typename T>
+__device__ __forceinline__ void slice_dot(uint32_t slot_s, int R, int K, uint32_t xs_s,
+                                          float* part, int warp, int lane) {
+  const int NC = K / kKC;
+  const int NG = (R + kRG - 1) / kRG;
+  for (int it = warp; it < NC * NG; it += kCons / 32) {
+    const int c = it % NC, g = it / NC;
+    float x[8];
+    {
+      const uint32_t xa = xs_s + (uint32_t)(c * kKC + lane * 8) * 4u;
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                   : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3]) : "r"(xa));
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                   : "=f"(x[4]), "=f"(x[5]), "=f"(x[6]), "=f"(x[7]) : "r"(xa + 16u));
     }
+    uint4 u[kRG];
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      if (i >= nr) break;
+    for (int i = 0; i < kRG; ++i) {
+      const int r = min(g * kRG + i, R - 1);  // rows past R: a valid row, result dropped
+      const uint32_t wa = slot_s + (uint32_t)((size_t)r * K + c * kKC + lane * 8) * 2u;
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(u[i].x), "=r"(u[i].y), "=r"(u[i].z), "=r"(u[i].w) : "r"(wa));
+    }
+    float acc[kRG];
+#pragma unroll
+    for (int i = 0; i < kRG; ++i) {
       float f[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(wr[i] + k), f);
-      float v = acc[i];
-      v = fmaf(f[0], a.x, v); v = fmaf(f[1], a.y, v); v = fmaf(f[2], a.z, v);
-      v = fmaf(f[3], a.w, v); v = fmaf(f[4], b.x, v); v = fmaf(f[5], b.y, v);
-      v = fmaf(f[6], b.z, v); v = fmaf(f[7], b.w, v);
-      acc[i] = v;
+      unpack8<T>(u[i], f);
+      float v0 = f[0] * x[0], v1 = f[1] * x[1];
+      v0 = fmaf(f[2], x[2], v0); v1 = fmaf(f[3], x[3], v1);
+      v0 = fmaf(f[4], x[4], v0); v1 = fmaf(f[5], x[5], v1);
+      v0 = fmaf(f[6], x[6], v0); v1 = fmaf(f[7], x[7], v1);
+      acc[i] = v0 + v1;
     }
+    // lanes with bit 4 set keep rows 2, 3 and send rows 0, 1; then bit 3
+    // picks one of the two; three more levels finish the sum
+    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+    float k0 = hi16 ? acc[2] : acc[0], k1 = hi16 ? acc[3] : acc[1];
+    k0 += __shfl_xor_sync(0xffffffffu, hi16 ? acc[0] : acc[2], 16);
+    k1 += __shfl_xor_sync(0xffffffffu, hi16 ? acc[1] : acc[3], 16);
+    float v = hi8 ? k1 : k0;
+    v += __shfl_xor_sync(0xffffffffu, hi8 ? k0 : k1, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    const int row = g * kRG + (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
+    if ((lane & 7) == 0 && row < R) part[c * R + row] = v;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-    for (int i = 0; i < NR; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-    if (SS) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-  }
-#pragma unroll
-  for (int i = 0; i < NR; ++i) out[i] = acc[i];
-  ss = s2;
+}
+
+// Row r's full dot product: its chunk partials summed in chunk order.
+__device__ __forceinline__ float row_sum(const float* part, int R, int K, int r) {
+  float t = 0.f;
+  for (int c = 0; c < K / kKC; ++c) t += part[c * R + r];
+  return t;
 }
 
 // Contiguous share [r0, r1) of `rows` for CTA c of G.
@@ -355,6 +387,7 @@ struct Smem {
   float mrun[kMaxG], lrun[kMaxG], corr[kMaxG];
   float red[32];
   float xres[kMaxRes];        // this CTA's rows of the residual stream (o-proj / down rows)
+  float gpart[kMaxPart];      // GEMV chunk partials of the current phase
   float best_v[16];
   int best_i[16];
   uint64_t full[2], empty[2];
@@ -368,21 +401,6 @@ struct Smem {
   int issued;                 // jobs the producer issued
 };
 
-template <typename T>
-__device__ float block_sumsq(Smem& sm, int n, int ctid) {
-  float p = 0.f;
-  for (int i = ctid; i < n; i += kCons) p += sm.xs[i] * sm.xs[i];
-  p = warp_sum(p);
-  if ((ctid & 31) == 0) sm.red[ctid >> 5] = p;
-  cons_sync();
-  if (ctid == 0) {
-    float t = 0.f;
-    for (int w = 0; w < kCons / 32; ++w) t += sm.red[w];
-    sm.red[31] = t;
-  }
-  cons_sync();
-  return sm.red[31];
-}
 
 template <typename T, int NG>
 __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) {
@@ -527,6 +545,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     const int R = (a.Hq + 2 * a.Hkv) * a.D;
     constexpr int GQ = NG;  // query heads per kv head
     const float inv_e = 1.f / (float)a.E;
+    const uint32_t xs_s = smem_u32(sm.xs);
     const void* emb_row = static_cast<const T*>(a.emb) + tok * a.E;
     const uint32_t o_bytes = job_of(a, 1, c, G).bytes0;
     const AttUnit au = att_unit(a, pos, c, G, o_bytes);
@@ -542,7 +561,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       {
         const uint8_t* sl = acquire();
         DP_TS(8 + l * 16 + 0);
-        load_vec<T>(sm.xs, xsrc, a.E, ctid);
+        load_vec<T>(sm.xs, xsrc, a.E, ctid, sm.red);
         cons_sync();
         DP_TS(8 + l * 16 + 14);
         {  // this CTA's residual rows, for the o-proj and down phases
@@ -551,27 +570,12 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           for (int i = ctid; i < e1 - e0; i += kCons) sm.xres[i] = sm.xs[e0 + i];
         }
         share(R, c, G, r0, r1);
-        // warp w: rows r0 + w + 15 i, four at a time
-#ifdef TPP_DP_REP
-        for (int rep = 0; rep < TPP_DP_REP; ++rep)
-#endif
-        for (int rb = r0 + warp; rb < r1 && ok; rb += kRG * (kCons / 32)) {
-          int rr[kRG];
-#pragma unroll
-          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
-          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
-          float v[kRG], ss;
-          rows_dot<T, kRG, true>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
-          const float rs = rsqrtf(ss * inv_e + a.eps);
-          if (lane < nr) {
-            float vi = v[0];
-#pragma unroll
-            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
-            static_cast<T*>(w.qkv)[rb + lane * (kCons / 32)] = from_f32<T>(vi * rs);
-          }
-        }
+        slice_dot<T>(smem_u32(sl), r1 - r0, a.E, xs_s, sm.gpart, warp, lane);
+        const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
         DP_TS(8 + l * 16 + 1);
         release();
+        for (int r = ctid; r < r1 - r0; r += kCons)
+          static_cast<T*>(w.qkv)[r0 + r] = from_f32<T>(row_sum(sm.gpart, r1 - r0, a.E, r) * rs);
       }
       if (!ok) break;
       grid_arrive(w, bar_target);
@@ -865,24 +869,13 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         cons_sync();
         DP_TS(8 + l * 16 + 15);
         share(a.E, c, G, r0, r1);
-        for (int rb = r0 + warp; rb < r1; rb += kRG * (kCons / 32)) {
-          int rr[kRG];
-#pragma unroll
-          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
-          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
-          float v[kRG], ss;
-          rows_dot<T, kRG, false>(sl, rr, nr, K, sm.xs, lane, v, ss);
-          if (lane < nr) {
-            float vi = v[0];
-#pragma unroll
-            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
-            const int lr = rr[0] + lane * (kCons / 32);
-            const T nv = from_f32<T>(sm.xres[lr] + vi);
-            static_cast<T*>(w.x)[r0 + lr] = nv;
-            sm.xres[lr] = to_f32(nv);
-          }
-        }
+        slice_dot<T>(smem_u32(sl), r1 - r0, K, xs_s, sm.gpart, warp, lane);
         release();
+        for (int r = ctid; r < r1 - r0; r += kCons) {
+          const T nv = from_f32<T>(sm.xres[r] + row_sum(sm.gpart, r1 - r0, K, r));
+          static_cast<T*>(w.x)[r0 + r] = nv;
+          sm.xres[r] = to_f32(nv);
+        }
       }
       DP_TS(8 + l * 16 + 6);
       if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 64)) { ok = false; break; }
@@ -890,39 +883,20 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       // ---- gate/up + SwiGLU: ff[f] = silu(g * rs) * (u * rs) ----
       {
         const uint8_t* sl = acquire();
-        load_vec<T>(sm.xs, w.x, a.E, ctid);
+        load_vec<T>(sm.xs, w.x, a.E, ctid, sm.red);
         cons_sync();
         DP_TS(8 + l * 16 + 8);
         share(a.F, c, G, r0, r1);
         const int nf = r1 - r0;
-        // warp w: features w + 15 i, kGF at a time (gate and up rows each)
-        constexpr int kGF = kRG >= 2 ? kRG / 2 : 1;
-#ifdef TPP_DP_REP
-        for (int rep = 0; rep < TPP_DP_REP; ++rep)
-#endif
-        for (int fb = warp; fb < nf; fb += kGF * (kCons / 32)) {
-          int rr[2 * kGF];
-#pragma unroll
-          for (int i = 0; i < kGF; ++i) {
-            rr[2 * i] = fb + i * (kCons / 32);
-            rr[2 * i + 1] = nf + fb + i * (kCons / 32);
-          }
-          const int nr = 2 * min(kGF, (nf - fb + kCons / 32 - 1) / (kCons / 32));
-          float v[2 * kGF], ss;
-          rows_dot<T, 2 * kGF, true>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
-          const float rs = rsqrtf(ss * inv_e + a.eps);
-          if (lane < nr / 2) {
-            float g = v[0], u = v[1];
-#pragma unroll
-            for (int i = 1; i < kGF; ++i) {
-              g = lane == i ? v[2 * i] : g;
-              u = lane == i ? v[2 * i + 1] : u;
-            }
-            static_cast<T*>(w.ff)[r0 + fb + lane * (kCons / 32)] =
-                from_f32<T>(act_silu(g * rs) * (u * rs));
-          }
-        }
+        // the slice: nf gate rows, then the nf up rows of the same features
+        slice_dot<T>(smem_u32(sl), 2 * nf, a.E, xs_s, sm.gpart, warp, lane);
+        const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
         release();
+        for (int f = ctid; f < nf; f += kCons) {
+          const float g = row_sum(sm.gpart, 2 * nf, a.E, f);
+          const float u = row_sum(sm.gpart, 2 * nf, a.E, nf + f);
+          static_cast<T*>(w.ff)[r0 + f] = from_f32<T>(act_silu(g * rs) * (u * rs));
+        }
       }
       DP_TS(8 + l * 16 + 9);
       if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 65)) { ok = false; break; }
@@ -934,24 +908,13 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         cons_sync();
         DP_TS(8 + l * 16 + 11);
         share(a.E, c, G, r0, r1);
-        for (int rb = r0 + warp; rb < r1; rb += kRG * (kCons / 32)) {
-          int rr[kRG];
-#pragma unroll
-          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - r0;
-          const int nr = min(kRG, (r1 - rb + kCons / 32 - 1) / (kCons / 32));
-          float v[kRG], ss;
-          rows_dot<T, kRG, false>(sl, rr, nr, a.F, sm.xs, lane, v, ss);
-          if (lane < nr) {
-            float vi = v[0];
-#pragma unroll
-            for (int i = 1; i < kRG; ++i) vi = lane == i ? v[i] : vi;
-            const int lr = rr[0] + lane * (kCons / 32);
-            const T nv = from_f32<T>(sm.xres[lr] + vi);
-            static_cast<T*>(w.x)[r0 + lr] = nv;
-            sm.xres[lr] = to_f32(nv);
-          }
-        }
+        slice_dot<T>(smem_u32(sl), r1 - r0, a.F, xs_s, sm.gpart, warp, lane);
         release();
+        for (int r = ctid; r < r1 - r0; r += kCons) {
+          const T nv = from_f32<T>(sm.xres[r] + row_sum(sm.gpart, r1 - r0, a.F, r));
+          static_cast<T*>(w.x)[r0 + r] = nv;
+          sm.xres[r] = to_f32(nv);
+        }
       }
       DP_TS(8 + l * 16 + 12);
       if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 66)) { ok = false; break; }
@@ -959,9 +922,9 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     }
     // ---- LM head: logits = (x . Wh_f) * rs, per-CTA argmax ----
     if (ok) {
-      load_vec<T>(sm.xs, w.x, a.E, ctid);
+      load_vec<T>(sm.xs, w.x, a.E, ctid, sm.red);
       cons_sync();
-      const float rs = rsqrtf(block_sumsq<T>(sm, a.E, ctid) * inv_e + a.eps);
+      const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
       int v0, v1;
       share(a.V, c, G, v0, v1);
       float bv = -INFINITY;
@@ -969,25 +932,22 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       for (int q = 0; jc < njobs && ok; ++q) {
         const uint8_t* sl = acquire();
         const int rr0 = v0 + q * a.lm_rows_per_job, rr1 = min(v1, rr0 + a.lm_rows_per_job);
-        for (int rb = rr0 + warp; rb < rr1; rb += kRG * (kCons / 32)) {
-          int rr[kRG];
-#pragma unroll
-          for (int i = 0; i < kRG; ++i) rr[i] = rb + i * (kCons / 32) - rr0;
-          const int nr = min(kRG, (rr1 - rb + kCons / 32 - 1) / (kCons / 32));
-          float v[kRG], ss;
-          rows_dot<T, kRG, false>(sl, rr, nr, a.E, sm.xs, lane, v, ss);
-          if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < kRG; ++i) {
-              if (i >= nr) break;
-              const int r = rb + i * (kCons / 32);
-              const float vi = rndT<T>(v[i] * rs);
-              static_cast<T*>(a.logits)[r] = from_f32<T>(vi);
-              if (vi > bv || (vi == bv && r < bi)) { bv = vi; bi = r; }
-            }
-          }
-        }
+        // partials of consecutive jobs alternate halves of gpart, so a job's
+        // epilogue can run while the next job's dot products are written
+        float* gp = sm.gpart + (q & 1) * (kMaxPart / 2);
+        slice_dot<T>(smem_u32(sl), rr1 - rr0, a.E, xs_s, gp, warp, lane);
         release();
+        for (int r = ctid; r < rr1 - rr0; r += kCons) {
+          const float vi = rndT<T>(row_sum(gp, rr1 - rr0, a.E, r) * rs);
+          static_cast<T*>(a.logits)[rr0 + r] = from_f32<T>(vi);
+          if (vi > bv || (vi == bv && rr0 + r < bi)) { bv = vi; bi = rr0 + r; }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
       }
       if (lane == 0) { sm.best_v[warp] = bv; sm.best_i[warp] = bi; }
       cons_sync();
@@ -1065,7 +1025,11 @@ bool persistent_fits(int64_t E, int64_t Hq, int64_t Hkv, int64_t D, int64_t F) {
   return D == 128 && (GQ == 1 || GQ == 2 || GQ == 4) && GQ + 2 <= kCons / 32 && GQ * D <= 2 * kCons && Hkv <= 64 &&
          E % 8 == 0 && F % 8 == 0 && E <= 3072 && Hq * D <= 3072 && F <= 3072 &&
          per(R) * E * 2 <= kSlot && per(E) * Hq * D * 2 <= kSlot && 2 * per(F) * E * 2 <= kSlot &&
-         per(E) * F * 2 <= kSlot && per(E) <= kMaxRes;
+         per(E) * F * 2 <= kSlot && per(E) <= kMaxRes &&
+         E % kKC == 0 && (Hq * D) % kKC == 0 && F % kKC == 0 &&
+         per(R) * (E / kKC) <= kMaxPart && 2 * per(F) * (E / kKC) <= kMaxPart &&
+         per(E) * (Hq * D / kKC) <= kMaxPart && per(E) * (F / kKC) <= kMaxPart &&
+         2 * (int64_t)(kSlot / (2 * E)) * (E / kKC) <= kMaxPart;
 }
 }  // namespace
 

@@ -66,7 +66,10 @@ __global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T* __restrict
       bi = i;
     }
   };
+  bool done = false;
+  if constexpr (sizeof(T) == 2) {  // 16-byte vectors of 8 elements (16-bit types only)
   if (vec) {
+    done = true;
     const int64_t nv = V / 8, per = (nv + kRowCtas - 1) / kRowCtas;
     const int64_t c0 = (int64_t)cr * per, c1 = c0 + per < nv ? c0 + per : nv;
     constexpr int step = kRowThreads;
@@ -94,7 +97,9 @@ __global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T* __restrict
     }
     if (cr == kRowCtas - 1)
       for (int64_t i = nv * 8 + threadIdx.x; i < V; i += kRowThreads) take(to_f32(row[i]), i);
-  } else {
+  }
+  }
+  if (!done) {
     const int64_t per = (V + kRowCtas - 1) / kRowCtas;
     const int64_t i0 = (int64_t)cr * per, i1 = i0 + per < V ? i0 + per : V;
     for (int64_t i = i0 + threadIdx.x; i < i1; i += kRowThreads) take(to_f32(row[i]), i);

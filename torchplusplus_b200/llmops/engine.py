@@ -135,13 +135,13 @@ class DecodeEngine:
             if max(ln["n"] for ln in self.lanes) > 32:
                 raise ValueError("fp8 decode weights serve lanes of at most 32 sequences")
             self.lm_head_f8 = ops.Fp8Weight(self.lm_head_f)
-        # batch 1, native weights, on request (persistent=True or
-        # TPP_PERSISTENT=1): the whole step as one persistent cooperative
-        # kernel (tpp_decode_step_persistent).  Off by default: measured
-        # 961 tok/s against 1155 for the launch-per-phase graph at batch 1.
+        # batch 1, native weights: the whole step as one persistent
+        # cooperative kernel (tpp_decode_step_persistent) unless turned off
+        # (persistent=False or TPP_PERSISTENT=0).  Qwen3-0.6B shape, context
+        # ~640: 743 us a step against 864 us for the launch-per-phase graph.
         self.persistent = None
         if persistent is None:
-            persistent = os.environ.get("TPP_PERSISTENT", "0") == "1"
+            persistent = os.environ.get("TPP_PERSISTENT", "1") != "0"
         if persistent and B == 1 and weight_format == "native" and \
                 self.cos.dtype == torch.float16:
             try:
