@@ -390,9 +390,16 @@ int tpp_decode_advance(const int64_t* next_tokens, int64_t* out_ids, int64_t ld_
                        void* stream);
 
 /* ---- persistent single-sequence decode step ------------------------------- */
+/* Row pitch of the persistent step's weights: `in` + TPP_PERSISTENT_ROW_PAD
+ * elements.  The padding (never read) shifts consecutive rows by 16
+ * shared-memory banks, so the kernel's tensor-core operand loads from a
+ * bulk-copied weight slice are conflict-free. */
+#define TPP_PERSISTENT_ROW_PAD 32
+
 /* One decoder layer's operands for tpp_decode_step_persistent (device
  * pointers; the array of these lives in device memory).  Weights are
- * [out, in] row-major in the step's dtype, with the RMSNorm weight in front
+ * [out, in] row-major in the step's dtype with a row pitch of
+ * in + TPP_PERSISTENT_ROW_PAD elements, with the RMSNorm weight in front
  * of a projection folded into it (w[r, k] * gamma[k]): wqkv [(Hq+2Hkv)*D, E]
  * (q rows, k rows, v rows), wo [E, Hq*D], wgu [2F, E] (gate rows, then up
  * rows), wdown [E, F]; qn / kn the per-head q / k RMSNorm weights [D] (may
@@ -421,7 +428,7 @@ int64_t tpp_decode_step_persistent_workspace(int64_t E, int64_t Hq, int64_t Hkv,
  * 0..positions[0] (split over CTAs, merged by every CTA that needs it) ->
  * o-proj + residual -> RMSNorm + gate/up + SwiGLU -> down + residual] ->
  * final RMSNorm + LM head (lm_head = W_head * final-norm weight, logits
- * written, [V] in dtype) -> argmax -> tokens[0] = next, out_ids[p+1] = next
+ * written, [V] in dtype; pitch E + TPP_PERSISTENT_ROW_PAD) -> argmax -> tokens[0] = next, out_ids[p+1] = next
  * (if p+1 < out_cap), positions[0] = p+1, seqlens[0] = p+2.  The phases are
  * separated by grid-wide barriers (bounded waits; an expiry raises the
  * device error flag and the kernel returns) instead of kernel boundaries,

@@ -26,6 +26,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include "tc_common.cuh"
+#include "mma_common.cuh"
 
 namespace tpp {
 namespace {
@@ -40,7 +41,8 @@ constexpr int kMaxCTAs = 256;
 constexpr int kPaceMax = 8;
 constexpr int kMaxRes = 64;              // residual rows per CTA (at most)
 constexpr int kRG = 4;                   // rows of one GEMV work item
-constexpr int kKC = 256;                 // K elements of one GEMV work item (8 a lane)
+constexpr int kKC = 256;                 // K elements of one GEMV work item
+constexpr int kPad = TPP_PERSISTENT_ROW_PAD;  // weight row pitch = K + kPad elements
 constexpr int kMaxPart = 512;            // GEMV partial sums per phase (chunks x rows)
 constexpr uint32_t kSpinLimit = 1u << 24;
 
@@ -179,21 +181,24 @@ __device__ __forceinline__ float ldT(const void* p, int64_t i) {
 template <typename T>
 __device__ __forceinline__ float rndT(float v) { return to_f32(from_f32<T>(v)); }
 
-// xs[0..n) = src[0..n) (dtype -> fp32), 8 elements (16 bytes) per load.
-// With red != nullptr each warp also leaves its share of sum(x^2) in
-// red[warp] (read back with sumsq_of after the next consumer barrier).
+// xh[0..n) = src[0..n) (the step's dtype, copied as is), 16 bytes per
+// load.  With red != nullptr each warp also leaves its share of sum(x^2)
+// (fp32) in red[warp] (read back with sumsq_of after the next consumer
+// barrier).
 template <typename T>
-__device__ __forceinline__ void load_vec(float* xs, const void* src, int n, int ctid,
+__device__ __forceinline__ void load_vec(uint16_t* xh, const void* src, int n, int ctid,
                                          float* red = nullptr) {
   const uint4* p = static_cast<const uint4*>(src);
   float ss = 0.f;
   for (int i = ctid; i < n / 8; i += kCons) {
-    float f[8];
-    unpack8<T>(__ldcg(p + i), f);
+    const uint4 u = __ldcg(p + i);
+    if (red != nullptr) {
+      float f[8];
+      unpack8<T>(u, f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-    *reinterpret_cast<float4*>(xs + 8 * i) = make_float4(f[0], f[1], f[2], f[3]);
-    *reinterpret_cast<float4*>(xs + 8 * i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+    reinterpret_cast<uint4*>(xh)[i] = u;
   }
   if (red != nullptr) {
     ss = warp_sum(ss);
@@ -207,62 +212,62 @@ __device__ __forceinline__ float sumsq_of(const float* red) {
   return t;
 }
 
-// Partial GEMV of this CTA's weight slice: rows [0, R) of a [R][K] slice in
-// shared memory (row stride K elements) dotted with x (fp32, shared).  The
-// work is cut into items of one 256-wide K chunk c x kRG rows; a consumer
-// warp takes items w, w + 15, ...; lane l holds x[256c + 8l, +8) in
-// registers, so x is read from shared memory once per item (not once per
-// row) and every weight byte once.  The kRG row sums are reduced across the
-// warp with a transposing butterfly (6 shuffles for 4 rows) and lane 8i
-// writes part[c * R + row i].  Callers sum the K/256 chunk partials of a row
-// in chunk order after a consumer barrier.
+// Partial GEMV of this CTA's weight slice on the tensor cores: rows [0, R)
+// of a slice in shared memory with row pitch K + kPad elements, times x (the
+// step's dtype, shared).  Work item (c, tile): 256-wide K chunk c x 16 rows;
+// a consumer warp takes items w, w + 15, ...  Per 32-wide k block a lane
+// loads 16 contiguous bytes (k = 8t .. 8t+7, t = lane % 4) of rows g and
+// g + 8 (g = lane / 4) and of x, and feeds them to two m16n8k16 MMAs with
+// the weights as A (16 rows x 16 k) and x as B (the same x in all 8
+// columns): the k order inside a block is permuted the same way for both
+// operands (physical 8t + {0,1,2,3} = logical {2t, 2t+1, 2t+8, 2t+9} of the
+// first MMA, 8t + {4..7} of the second), so each MMA sees every k of its
+// 16 once.  The 64-byte row padding puts rows g and g+1 16 banks apart: the
+// 16-byte loads are conflict-free.  Lane 4g holds the fp32 sums of rows g
+// (d[0]) and g + 8 (d[2]) and writes part[c * R + row].  Callers sum the
+// K/256 chunk partials of a row in chunk order after a consumer barrier.
 template <typename T>
-__device__ __forceinline__ void slice_dot(uint32_t slot_s, int R, int K, uint32_t xs_s,
+__device__ __forceinline__ void slice_dot(uint32_t slot_s, int R, int K, uint32_t xh_s,
                                           float* part, int warp, int lane) {
   const int NC = K / kKC;
-  const int NG = (R + kRG - 1) / kRG;
-  for (int it = warp; it < NC * NG; it += kCons / 32) {
-    const int c = it % NC, g = it / NC;
-    float x[8];
-    {
-      const uint32_t xa = xs_s + (uint32_t)(c * kKC + lane * 8) * 4u;
-      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                   : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3]) : "r"(xa));
-      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                   : "=f"(x[4]), "=f"(x[5]), "=f"(x[6]), "=f"(x[7]) : "r"(xa + 16u));
+  const int NT = (R + 15) / 16;
+  const uint32_t pitch = (uint32_t)(K + kPad) * 2u;
+  const int g = lane >> 2, t = lane & 3;
+  // item it = tile * NC + c, stepped by 15 without a division per item
+  int c = warp % NC, tile = warp / NC;
+  for (int it = warp; it < NC * NT; it += kCons / 32) {
+    if (it != warp) {
+      c += kCons / 32;
+      while (c >= NC) { c -= NC; ++tile; }
     }
-    uint4 u[kRG];
-#pragma unroll
-    for (int i = 0; i < kRG; ++i) {
-      const int r = min(g * kRG + i, R - 1);  // rows past R: a valid row, result dropped
-      const uint32_t wa = slot_s + (uint32_t)((size_t)r * K + c * kKC + lane * 8) * 2u;
+    const int ra = tile * 16 + g, rb = ra + 8;
+    // rows past R read a valid row; their sums are dropped
+    const uint32_t koff = (uint32_t)(c * kKC + 8 * t) * 2u;
+    const uint32_t wa = slot_s + (uint32_t)min(ra, R - 1) * pitch + koff;
+    const uint32_t wb = slot_s + (uint32_t)min(rb, R - 1) * pitch + koff;
+    const uint32_t xa = xh_s + koff;
+    // two accumulators: the two MMAs of a k block do not wait on each other
+    float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int kb = 0; kb < kKC / 32; ++kb) {
+      uint32_t A0[4], A1[4], X[4];
       asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(u[i].x), "=r"(u[i].y), "=r"(u[i].z), "=r"(u[i].w) : "r"(wa));
+                   : "=r"(A0[0]), "=r"(A0[1]), "=r"(A0[2]), "=r"(A0[3]) : "r"(wa + kb * 64));
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(A1[0]), "=r"(A1[1]), "=r"(A1[2]), "=r"(A1[3]) : "r"(wb + kb * 64));
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(X[0]), "=r"(X[1]), "=r"(X[2]), "=r"(X[3]) : "r"(xa + kb * 64));
+      const uint32_t a0[4] = {A0[0], A1[0], A0[1], A1[1]};
+      mma<T>(d, a0, X[0], X[1]);
+      const uint32_t a1[4] = {A0[2], A1[2], A0[3], A1[3]};
+      mma<T>(e, a1, X[2], X[3]);
     }
-    float acc[kRG];
-#pragma unroll
-    for (int i = 0; i < kRG; ++i) {
-      float f[8];
-      unpack8<T>(u[i], f);
-      float v0 = f[0] * x[0], v1 = f[1] * x[1];
-      v0 = fmaf(f[2], x[2], v0); v1 = fmaf(f[3], x[3], v1);
-      v0 = fmaf(f[4], x[4], v0); v1 = fmaf(f[5], x[5], v1);
-      v0 = fmaf(f[6], x[6], v0); v1 = fmaf(f[7], x[7], v1);
-      acc[i] = v0 + v1;
+    d[0] += e[0];
+    d[2] += e[2];
+    if (t == 0) {
+      if (ra < R) part[c * R + ra] = d[0];
+      if (rb < R) part[c * R + rb] = d[2];
     }
-    // lanes with bit 4 set keep rows 2, 3 and send rows 0, 1; then bit 3
-    // picks one of the two; three more levels finish the sum
-    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
-    float k0 = hi16 ? acc[2] : acc[0], k1 = hi16 ? acc[3] : acc[1];
-    k0 += __shfl_xor_sync(0xffffffffu, hi16 ? acc[0] : acc[2], 16);
-    k1 += __shfl_xor_sync(0xffffffffu, hi16 ? acc[1] : acc[3], 16);
-    float v = hi8 ? k1 : k0;
-    v += __shfl_xor_sync(0xffffffffu, hi8 ? k0 : k1, 8);
-    v += __shfl_xor_sync(0xffffffffu, v, 4);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    const int row = g * kRG + (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
-    if ((lane & 7) == 0 && row < R) part[c * R + row] = v;
   }
 }
 
@@ -273,10 +278,25 @@ __device__ __forceinline__ float row_sum(const float* part, int R, int K, int r)
   return t;
 }
 
-// Contiguous share [r0, r1) of `rows` for CTA c of G.
+// Contiguous share [r0, r1) of `rows` for CTA c of G (32-bit: rows * G
+// stays below 2^32 for every plan this kernel accepts).
 __device__ __forceinline__ void share(int rows, int c, int G, int& r0, int& r1) {
-  r0 = (int)((int64_t)rows * c / G);
-  r1 = (int)((int64_t)rows * (c + 1) / G);
+  r0 = (int)((uint32_t)rows * (uint32_t)c / (uint32_t)G);
+  r1 = (int)((uint32_t)rows * (uint32_t)(c + 1) / (uint32_t)G);
+}
+// This CTA's row ranges of every phase, computed once per launch (integer
+// division is a multi-instruction routine): QKV rows, E rows (o-proj, down,
+// residual), F features (gate/up), V rows (LM head).
+struct Shares {
+  int q0, q1, e0, e1, f0, f1, v0, v1;
+};
+__device__ __forceinline__ Shares shares_of(int R, int E, int F, int V, int c, int G) {
+  Shares h;
+  share(R, c, G, h.q0, h.q1);
+  share(E, c, G, h.e0, h.e1);
+  share(F, c, G, h.f0, h.f1);
+  share(V, c, G, h.v0, h.v1);
+  return h;
 }
 
 
@@ -290,7 +310,7 @@ struct Job {
   uint32_t bytes1;
 };
 
-__device__ __forceinline__ Job job_of(const StepArgs& a, int j, int c, int G) {
+__device__ __forceinline__ Job job_of(const StepArgs& a, int j, const Shares& h) {
   Job jb = {nullptr, 0, nullptr, 0};
   const int esz = 2;
   if (j < 4 * a.n_layers) {
@@ -298,48 +318,45 @@ __device__ __forceinline__ Job job_of(const StepArgs& a, int j, int c, int G) {
     int r0, r1;
     switch (j % 4) {
       case 0: {
-        share((a.Hq + 2 * a.Hkv) * a.D, c, G, r0, r1);
-        jb.src0 = static_cast<const uint8_t*>(L.wqkv) + (size_t)r0 * a.E * esz;
-        jb.bytes0 = (uint32_t)((r1 - r0) * a.E * esz);
+        r0 = h.q0; r1 = h.q1;
+        jb.src0 = static_cast<const uint8_t*>(L.wqkv) + (size_t)r0 * (a.E + kPad) * esz;
+        jb.bytes0 = (uint32_t)((r1 - r0) * (a.E + kPad) * esz);
         break;
       }
       case 1: {
-        share(a.E, c, G, r0, r1);
-        jb.src0 = static_cast<const uint8_t*>(L.wo) + (size_t)r0 * a.Hq * a.D * esz;
-        jb.bytes0 = (uint32_t)((r1 - r0) * a.Hq * a.D * esz);
+        r0 = h.e0; r1 = h.e1;
+        jb.src0 = static_cast<const uint8_t*>(L.wo) + (size_t)r0 * (a.Hq * a.D + kPad) * esz;
+        jb.bytes0 = (uint32_t)((r1 - r0) * (a.Hq * a.D + kPad) * esz);
         break;
       }
       case 2: {
-        share(a.F, c, G, r0, r1);
-        jb.src0 = static_cast<const uint8_t*>(L.wgu) + (size_t)r0 * a.E * esz;
-        jb.bytes0 = (uint32_t)((r1 - r0) * a.E * esz);
-        jb.src1 = static_cast<const uint8_t*>(L.wgu) + (size_t)(a.F + r0) * a.E * esz;
+        r0 = h.f0; r1 = h.f1;
+        jb.src0 = static_cast<const uint8_t*>(L.wgu) + (size_t)r0 * (a.E + kPad) * esz;
+        jb.bytes0 = (uint32_t)((r1 - r0) * (a.E + kPad) * esz);
+        jb.src1 = static_cast<const uint8_t*>(L.wgu) + (size_t)(a.F + r0) * (a.E + kPad) * esz;
         jb.bytes1 = jb.bytes0;
         break;
       }
       default: {
-        share(a.E, c, G, r0, r1);
-        jb.src0 = static_cast<const uint8_t*>(L.wdown) + (size_t)r0 * a.F * esz;
-        jb.bytes0 = (uint32_t)((r1 - r0) * a.F * esz);
+        r0 = h.e0; r1 = h.e1;
+        jb.src0 = static_cast<const uint8_t*>(L.wdown) + (size_t)r0 * (a.F + kPad) * esz;
+        jb.bytes0 = (uint32_t)((r1 - r0) * (a.F + kPad) * esz);
         break;
       }
     }
   } else {
-    int v0, v1;
-    share(a.V, c, G, v0, v1);
+    const int v0 = h.v0, v1 = h.v1;
     const int q = j - 4 * a.n_layers;
     const int r0 = v0 + q * a.lm_rows_per_job;
     const int r1 = min(v1, r0 + a.lm_rows_per_job);
-    jb.src0 = static_cast<const uint8_t*>(a.lm_head) + (size_t)r0 * a.E * esz;
-    jb.bytes0 = r1 > r0 ? (uint32_t)((r1 - r0) * a.E * esz) : 0u;
+    jb.src0 = static_cast<const uint8_t*>(a.lm_head) + (size_t)r0 * (a.E + kPad) * esz;
+    jb.bytes0 = r1 > r0 ? (uint32_t)((r1 - r0) * (a.E + kPad) * esz) : 0u;
   }
   return jb;
 }
 
-__device__ __forceinline__ int n_jobs(const StepArgs& a, int c, int G) {
-  int v0, v1;
-  share(a.V, c, G, v0, v1);
-  return 4 * a.n_layers + (v1 - v0 + a.lm_rows_per_job - 1) / a.lm_rows_per_job;
+__device__ __forceinline__ int n_jobs(const StepArgs& a, const Shares& h) {
+  return 4 * a.n_layers + (h.v1 - h.v0 + a.lm_rows_per_job - 1) / a.lm_rows_per_job;
 }
 
 
@@ -376,7 +393,7 @@ __device__ __forceinline__ AttUnit att_unit(const StepArgs& a, int pos, int c, i
 struct Smem {
   union {
     struct {
-      float xs[3072 + 64];    // the phase's input vector (fp32), >= max(E, Hq D, F)
+      uint16_t xh[3072 + 64]; // the phase's input vector (step dtype), >= max(E, Hq D, F)
       float q[kMaxG][128];    // attention: normed + rotated q rows
       float knew[128], vnew[128];
       float sc[kMaxG][kTK];   // scores / probabilities of one key tile
@@ -413,7 +430,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
   ws_layout(a.ws, a.E, a.Hq, a.Hkv, a.D, a.F, &w);
   const int c = blockIdx.x, G = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int njobs = n_jobs(a, c, G);
+  const Shares sh = shares_of((a.Hq + 2 * a.Hkv) * a.D, a.E, a.F, a.V, c, G);
+  const int njobs = n_jobs(a, sh);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -456,7 +474,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       // norm weights, after the weights (they depend on nothing in the
       // step), on their own barrier
       const int ppos = a.positions[0];
-      const AttUnit pu = att_unit(a, ppos, c, G, job_of(a, 1, c, G).bytes0);
+      const AttUnit pu = att_unit(a, ppos, c, G, job_of(a, 1, sh).bytes0);
       int kv_issued = 0;
       auto stage_kv = [&](int j, uint8_t* dst) {
         if (!pu.in_att || j >= 4 * a.n_layers || (j & 3) != 1) return;
@@ -483,7 +501,7 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           }
           if (!got) break;
         }
-        const Job jb = job_of(a, j, c, G);
+        const Job jb = job_of(a, j, sh);
         if (depth == 0 || j >= 4 * a.n_layers) {
           mbar_arrive_expect_tx(&sm.full[s], jb.bytes0 + jb.bytes1);
           if (jb.bytes0) bulk_load(slot[s], jb.src0, jb.bytes0, &sm.full[s]);
@@ -545,9 +563,9 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     const int R = (a.Hq + 2 * a.Hkv) * a.D;
     constexpr int GQ = NG;  // query heads per kv head
     const float inv_e = 1.f / (float)a.E;
-    const uint32_t xs_s = smem_u32(sm.xs);
+    const uint32_t xs_s = smem_u32(sm.xh);
     const void* emb_row = static_cast<const T*>(a.emb) + tok * a.E;
-    const uint32_t o_bytes = job_of(a, 1, c, G).bytes0;
+    const uint32_t o_bytes = job_of(a, 1, sh).bytes0;
     const AttUnit au = att_unit(a, pos, c, G, o_bytes);
     int kv_waited = 0;
     for (int i = ctid; i < 256; i += kCons)
@@ -561,15 +579,15 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       {
         const uint8_t* sl = acquire();
         DP_TS(8 + l * 16 + 0);
-        load_vec<T>(sm.xs, xsrc, a.E, ctid, sm.red);
+        load_vec<T>(sm.xh, xsrc, a.E, ctid, sm.red);
         cons_sync();
         DP_TS(8 + l * 16 + 14);
         {  // this CTA's residual rows, for the o-proj and down phases
-          int e0, e1;
-          share(a.E, c, G, e0, e1);
-          for (int i = ctid; i < e1 - e0; i += kCons) sm.xres[i] = sm.xs[e0 + i];
+          const int e0 = sh.e0, e1 = sh.e1;
+          for (int i = ctid; i < e1 - e0; i += kCons)
+            sm.xres[i] = to_f32(reinterpret_cast<const T*>(sm.xh)[e0 + i]);
         }
-        share(R, c, G, r0, r1);
+        r0 = sh.q0; r1 = sh.q1;
         slice_dot<T>(smem_u32(sl), r1 - r0, a.E, xs_s, sm.gpart, warp, lane);
         const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
         DP_TS(8 + l * 16 + 1);
@@ -865,10 +883,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         const uint8_t* sl = acquire();
         DP_TS(8 + l * 16 + 5);
         const int K = a.Hq * a.D;
-        load_vec<T>(sm.xs, w.o, K, ctid);
+        load_vec<T>(sm.xh, w.o, K, ctid);
         cons_sync();
         DP_TS(8 + l * 16 + 15);
-        share(a.E, c, G, r0, r1);
+        r0 = sh.e0; r1 = sh.e1;
         slice_dot<T>(smem_u32(sl), r1 - r0, K, xs_s, sm.gpart, warp, lane);
         release();
         for (int r = ctid; r < r1 - r0; r += kCons) {
@@ -883,10 +901,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       // ---- gate/up + SwiGLU: ff[f] = silu(g * rs) * (u * rs) ----
       {
         const uint8_t* sl = acquire();
-        load_vec<T>(sm.xs, w.x, a.E, ctid, sm.red);
+        load_vec<T>(sm.xh, w.x, a.E, ctid, sm.red);
         cons_sync();
         DP_TS(8 + l * 16 + 8);
-        share(a.F, c, G, r0, r1);
+        r0 = sh.f0; r1 = sh.f1;
         const int nf = r1 - r0;
         // the slice: nf gate rows, then the nf up rows of the same features
         slice_dot<T>(smem_u32(sl), 2 * nf, a.E, xs_s, sm.gpart, warp, lane);
@@ -904,10 +922,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       // ---- down + residual: x[r] = x[r] + ff . Wd[r] ----
       {
         const uint8_t* sl = acquire();
-        load_vec<T>(sm.xs, w.ff, a.F, ctid);
+        load_vec<T>(sm.xh, w.ff, a.F, ctid);
         cons_sync();
         DP_TS(8 + l * 16 + 11);
-        share(a.E, c, G, r0, r1);
+        r0 = sh.e0; r1 = sh.e1;
         slice_dot<T>(smem_u32(sl), r1 - r0, a.F, xs_s, sm.gpart, warp, lane);
         release();
         for (int r = ctid; r < r1 - r0; r += kCons) {
@@ -922,11 +940,10 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     }
     // ---- LM head: logits = (x . Wh_f) * rs, per-CTA argmax ----
     if (ok) {
-      load_vec<T>(sm.xs, w.x, a.E, ctid, sm.red);
+      load_vec<T>(sm.xh, w.x, a.E, ctid, sm.red);
       cons_sync();
       const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
-      int v0, v1;
-      share(a.V, c, G, v0, v1);
+      const int v0 = sh.v0, v1 = sh.v1;
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       for (int q = 0; jc < njobs && ok; ++q) {
@@ -1024,12 +1041,13 @@ bool persistent_fits(int64_t E, int64_t Hq, int64_t Hkv, int64_t D, int64_t F) {
   auto per = [&](int64_t rows) { return (rows + G - 1) / G; };
   return D == 128 && (GQ == 1 || GQ == 2 || GQ == 4) && GQ + 2 <= kCons / 32 && GQ * D <= 2 * kCons && Hkv <= 64 &&
          E % 8 == 0 && F % 8 == 0 && E <= 3072 && Hq * D <= 3072 && F <= 3072 &&
-         per(R) * E * 2 <= kSlot && per(E) * Hq * D * 2 <= kSlot && 2 * per(F) * E * 2 <= kSlot &&
-         per(E) * F * 2 <= kSlot && per(E) <= kMaxRes &&
+         per(R) * (E + kPad) * 2 <= kSlot && per(E) * (Hq * D + kPad) * 2 <= kSlot &&
+         2 * per(F) * (E + kPad) * 2 <= kSlot && per(E) * (F + kPad) * 2 <= kSlot &&
+         per(E) <= kMaxRes &&
          E % kKC == 0 && (Hq * D) % kKC == 0 && F % kKC == 0 &&
          per(R) * (E / kKC) <= kMaxPart && 2 * per(F) * (E / kKC) <= kMaxPart &&
          per(E) * (Hq * D / kKC) <= kMaxPart && per(E) * (F / kKC) <= kMaxPart &&
-         2 * (int64_t)(kSlot / (2 * E)) * (E / kKC) <= kMaxPart;
+         2 * (int64_t)(kSlot / (2 * (E + kPad))) * (E / kKC) <= kMaxPart;
 }
 }  // namespace
 
@@ -1068,7 +1086,7 @@ extern "C" int tpp_decode_step_persistent(
   a.E = (int)E; a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.D = (int)D; a.F = (int)F; a.V = (int)V;
   a.Smax = (int)Smax; a.eps = eps;
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
-  a.lm_rows_per_job = (int)(kSlot / (E * 2));
+  a.lm_rows_per_job = (int)(kSlot / ((E + kPad) * 2));
   // TPP_DP_PACE="<chunk KiB>,<chunks in flight>" (",0": one burst per slice)
   a.pace_chunk = 8 * 1024;
   a.pace_depth = 6;

@@ -350,12 +350,17 @@ def l2_prefetch(t: torch.Tensor) -> None:
     N.call("tpp_l2_prefetch", t.data_ptr(), n - n % 16, N.stream_of(t))
 
 
+PERSISTENT_ROW_PAD = 32  # TPP_PERSISTENT_ROW_PAD (include/tpp_b200.h)
+
+
 class PersistentDecode:
     """Operands of tpp_decode_step_persistent for one sequence: the per-layer
     pointer table (tpp_decode_layer records, in device memory) and the
     zero-initialised workspace.  `layers` holds per layer the folded QKV
     weight, q/k norm weights, o-proj weight, folded gate/up weight, down
-    weight and the layer's [Hkv, Smax, D] K and V caches."""
+    weight and the layer's [Hkv, Smax, D] K and V caches.  The projection
+    and LM-head weights are copied once into the kernel's padded layout (row
+    pitch in + PERSISTENT_ROW_PAD elements)."""
 
     def __init__(self, layers: list, emb: torch.Tensor, lm_head_folded: torch.Tensor,
                  cos: torch.Tensor, sin: torch.Tensor, Hq: int, Hkv: int, D: int, Smax: int,
@@ -365,9 +370,18 @@ class PersistentDecode:
         if cos.dtype != torch.float16 or sin.dtype != torch.float16 or cos.shape[1] != D:
             raise ValueError("RoPE tables must be fp16 [ctx, D]")
         dev = emb.device
+        nbytes = int(N.lib().tpp_decode_step_persistent_workspace(
+            emb.shape[1], Hq, Hkv, D, layers[0]["wgu"].shape[0] // 2, Smax))
+        if nbytes <= 0:
+            raise ValueError("model shape outside the persistent decode plan")
+        # weights in the kernel's layout: row pitch in + TPP_PERSISTENT_ROW_PAD
+        pad = lambda w: torch.nn.functional.pad(w, (0, PERSISTENT_ROW_PAD)).contiguous()
+        lm_head_folded = pad(lm_head_folded)
         self.keep = [emb, lm_head_folded, cos, sin]
         ptrs = []
         for L in layers:
+            L = dict(L, wqkv=pad(L["wqkv"]), wo=pad(L["wo"]), wgu=pad(L["wgu"]),
+                     wdown=pad(L["wdown"]))
             for t in (L["wqkv"], L["qn"], L["kn"], L["wo"], L["wgu"], L["wdown"], L["kc"], L["vc"]):
                 if t is not None:
                     _same_dtype(emb, t)
@@ -382,9 +396,6 @@ class PersistentDecode:
         self.V = lm_head_folded.shape[0]
         self.F = layers[0]["wgu"].shape[0] // 2
         self.Hq, self.Hkv, self.D, self.Smax, self.eps = Hq, Hkv, D, Smax, eps
-        nbytes = int(N.lib().tpp_decode_step_persistent_workspace(self.E, Hq, Hkv, D, self.F, Smax))
-        if nbytes <= 0:
-            raise ValueError("model shape outside the persistent decode plan")
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         self.emb, self.lm_head, self.cos, self.sin = emb, lm_head_folded, cos, sin
 
