@@ -388,7 +388,8 @@ def per_op(hbm_peak: float, tc_peak: float) -> dict:
 
 ONE_OPS = ("rmsnorm", "linear_silu", "qkrope", "attention_prefill", "prefill_attn_d64",
            "hgemv_lm_head", "hgemv_k1024_n3072", "decode_linears", "decode_attention",
-           "qk_norm_rope_cache", "swa_decode", "argmax", "sample", "embedding", "lm_head_fp8")
+           "qk_norm_rope_cache", "swa_decode", "argmax", "sample", "embedding", "lm_head_fp8",
+           "decode_step_b1")
 
 
 def one_op(name: str, reps: int) -> dict:
@@ -488,6 +489,21 @@ def one_op(name: str, reps: int) -> dict:
         x = rnd(32, 1024, dtype=bf)
         y = torch.empty(32, 151936, device=dev, dtype=bf)
         fn = lambda: ops.linear_fp8(x, W, eps=1e-6, out=y)  # noqa: E731
+    elif name == "decode_step_b1":   # persistent one-kernel decode step, batch 1, context 640
+        from torchplusplus_b200.llmops.engine import DecodeEngine
+        from torchplusplus_b200.llmops.qwen3 import Qwen3, Qwen3Config
+        cfg = Qwen3Config()
+        model = Qwen3(cfg, device=dev).init_weights(0.02, seed=0)
+        ids = torch.randint(0, cfg.vocab_size, (1, 640), generator=torch.Generator().manual_seed(1))
+        with torch.inference_mode():
+            eng = DecodeEngine(model, 1, 640 + 64 * reps + 8, persistent=True)
+            if eng.persistent is None:
+                raise SystemExit("decode_step_b1: the persistent step is unavailable")
+            eng.prefill(ids)
+
+        def fn():
+            with torch.inference_mode():
+                eng.step_eager()
     else:
         raise SystemExit(f"--one-op: unknown op {name!r}; one of {', '.join(ONE_OPS)}")
     torch.cuda.synchronize()
