@@ -284,15 +284,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!valid) sv[i] = -INFINITY;
         }
       }
+      // row max: 8 independent chains of three-input max over the 64 keys
       float pm[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) pm[u] = sv[u];
+      for (int u = 0; u < 8; ++u) pm[u] = fmaxf(sv[u], sv[8 + u]);
 #pragma unroll
-      for (int i = 8; i < HK; i += 8)
+      for (int i = 16; i < HK; i += 16)
 #pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], sv[i + u]);
-      float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                       fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        for (int u = 0; u < 8; ++u) pm[u] = fmax3(pm[u], sv[i + u], sv[i + 8 + u]);
+      float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                       fmaxf(pm[6], pm[7]));
       // exchange with the other half of the row (slot by tile parity); also
       // orders every S load of this tile before any P store below (P of the
       // whole tile overwrites the first 64 S columns)
@@ -327,17 +328,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
       }
       // p = exp2(s * scale - m_ref); masked entries are -inf -> 0
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // pairs of keys on the two-lane fp32 pipe: scale and shift, then the
+      // two exponentials, then the running sums (4 pair accumulators)
+      uint64_t ps[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[HK / 2];
       const float nm = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2), nm2 = f2_pack(nm, nm);
 #pragma unroll
       for (int i = 0; i < HK; i += 2) {
-        const float p0 = exp2f(fmaf(sv[i], p.scale_log2, nm));
-        const float p1 = exp2f(fmaf(sv[i + 1], p.scale_log2, nm));
-        ps[(i >> 1) & 7] += p0 + p1;
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(sv[i], sv[i + 1]), sc2, nm2), a0, a1);
+        const float p0 = ex2_ftz(a0), p1 = ex2_ftz(a1);
+        const uint64_t pp = f2_pack(p0, p1);
+        ps[(i >> 1) & 3] = f2_add(ps[(i >> 1) & 3], pp);
         pk[i / 2] = pack2<T>(p0, p1);
       }
-      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      {
+        const uint64_t t2 = f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3]));
+        float t0, t1;
+        f2_unpack(t2, t0, t1);
+        l += t0 + t1;
+      }
       tmem_st32(tSb + hf * (HK / 2), pk);  // P columns of this half's keys
       tmem_wait_st();
       tc_fence_before();

@@ -131,6 +131,41 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Activations, fp32 in/out, following csrc/activation/activation.cuh:26-67
 // of the reference (GeLU-tanh with sqrt(2/pi) and 0.044715; SiLU x/(1+e^-x)).
+// 2^x with the hardware's approximate base-2 exponential (PTX ex2.approx,
+// flush-to-zero): one special-function instruction.  Relative error about
+// 2^-22 (PTX ISA bound); results below 2^-126 become 0, which a softmax
+// weight of that size is anyway.  -inf gives 0.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+// Packed pairs of fp32 (low word first) for the sm_100 two-lane fp32 ops.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// a * b + c and a + b on both lanes of packed fp32 pairs (round to nearest).
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ float act_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float act_gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
