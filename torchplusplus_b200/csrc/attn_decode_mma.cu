@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       corr[hr] = 1.f;
       if (mx > m_r[hr] + 8.f) {
-        corr[hr] = exp2f(m_r[hr] - mx);  // 0 when no key was seen yet
+        corr[hr] = ex2_ftz(m_r[hr] - mx);  // 0 when no key was seen yet
         m_r[hr] = mx;
         grow = true;
       }
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = sc[j][2 * hr + e];
-          const float pv = (v == -INFINITY) ? 0.f : exp2f(v - mx);
+          const float pv = (v == -INFINITY) ? 0.f : ex2_ftz(v - mx);
           sc[j][2 * hr + e] = pv;
           sum += pv;
         }
@@ -452,8 +452,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(
       const float sk = snew[g + hr * 8];
       if (sk == -INFINITY) continue;  // padding row
       const float mx = fmaxf(m_r[hr], sk);
-      const float corr = exp2f(m_r[hr] - mx);  // 0 when no key was seen yet
-      const float pn = exp2f(sk - mx);
+      const float corr = ex2_ftz(m_r[hr] - mx);  // 0 when no key was seen yet
+      const float pn = ex2_ftz(sk - mx);
       l_r[hr] = l_r[hr] * corr + (c == 0 ? pn : 0.f);  // l is summed over the quad
 #pragma unroll
       for (int d = 0; d < D / 8; ++d) {

@@ -743,13 +743,13 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
               const float mn = fmaxf(mo, m);
               float l = 0.f;
               for (int i = lane; i < nt; i += 32) {
-                const float pv = exp2f(sm.sc[warp][i] - mn);
+                const float pv = ex2_ftz(sm.sc[warp][i] - mn);
                 sm.sc[warp][i] = pv;
                 l += pv;
               }
               l = warp_sum(l);
               if (lane == 0) {
-                const float cr = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+                const float cr = mo == -INFINITY ? 0.f : ex2_ftz(mo - mn);
                 sm.corr[warp] = cr;
                 sm.lrun[warp] = sm.lrun[warp] * cr + l;
                 sm.mrun[warp] = mn;
