@@ -49,3 +49,11 @@ def test_argument_validation_needs_no_gpu():
     assert e.value.status == 6  # head dim 96 unsupported
     # decode workspace query is pure host arithmetic
     assert N.lib().tpp_attention_decode_workspace(1, 16, 8, 128) >= 0
+
+
+def test_persistent_row_pad_matches_header():
+    """The Python side pads the persistent step's weight copies by the pitch
+    the kernel expects (TPP_PERSISTENT_ROW_PAD)."""
+    from torchplusplus_b200 import ops
+    m = re.search(r"#define\s+TPP_PERSISTENT_ROW_PAD\s+(\d+)", HEADER.read_text())
+    assert m and int(m.group(1)) == ops.PERSISTENT_ROW_PAD
