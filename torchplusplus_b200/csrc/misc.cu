@@ -74,26 +74,23 @@ __global__ void __launch_bounds__(kRowThreads) argmax_kernel(const T* __restrict
     const int64_t c0 = (int64_t)cr * per, c1 = c0 + per < nv ? c0 + per : nv;
     constexpr int step = kRowThreads;
     int64_t c = c0 + threadIdx.x;
-    // four independent 16-byte loads in flight per thread (the logits were
-    // just written: each round trip is an L2 latency); order does not matter,
-    // ties are resolved by index
-    for (; c + 3 * step < c1; c += 4 * step) {
-      uint4 u[4];
+    // up to eight independent 16-byte loads in flight per thread: one
+    // memory round trip covers a row slice of up to 8 x 512 x 8 elements
+    // (the logits were just written: each round trip is an L2 latency);
+    // order does not matter, ties are resolved by index
+    for (; c < c1; c += 8 * step) {
+      uint4 u[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) u[q] = ldg_nc_v4(row + (c + q * step) * 8);
+      for (int q = 0; q < 8; ++q)
+        u[q] = c + q * step < c1 ? ldg_nc_v4(row + (c + q * step) * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 8; ++q) {
+        if (c + q * step >= c1) break;
         float f[8];
         unpack8<T>(u[q], f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) take(f[j], (c + q * step) * 8 + j);
       }
-    }
-    for (; c < c1; c += step) {
-      float f[8];
-      unpack8<T>(ldg_nc_v4(row + c * 8), f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) take(f[j], c * 8 + j);
     }
     if (cr == kRowCtas - 1)
       for (int64_t i = nv * 8 + threadIdx.x; i < V; i += kRowThreads) take(to_f32(row[i]), i);
