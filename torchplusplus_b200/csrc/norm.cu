@@ -28,13 +28,24 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(
     const T* __restrict__ x, int64_t ldx, T* res, const T* __restrict__ w,
     const T* __restrict__ b, T* __restrict__ y, int64_t ldy, int64_t rows, int cols,
     float eps) {
-  pdl_wait();
-  pdl_trigger();
   const int groups = blockDim.x / G;
   const int64_t row = (int64_t)blockIdx.x * groups + threadIdx.x / G;
   const int lane = threadIdx.x % G;
   const bool valid_row = row < rows;
   const int nvec = cols >> 3;
+  // gamma (and beta) do not depend on the previous kernel: requested before
+  // the dependency wait, so they are not a round trip after the reduction
+  uint4 gw[NV], bw[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * G;
+    const bool in = valid_row && c < nvec;
+    gw[i] = in ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0);
+    bw[i] = in && MODE == 2 && b != nullptr ? __ldg(reinterpret_cast<const uint4*>(b) + c)
+                                            : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  pdl_trigger();
 
   float v[NV][8];
 #pragma unroll
@@ -94,10 +105,9 @@ __global__ void __launch_bounds__(256) norm_rows_kernel(
   for (int i = 0; i < NV; ++i) {
     const int c = lane + i * G;
     if (c < nvec) {
-      float g[8], o[8];
-      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(w) + c), g);
-      float bb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (MODE == 2 && b != nullptr) unpack8<T>(__ldg(reinterpret_cast<const uint4*>(b) + c), bb);
+      float g[8], o[8], bb[8];
+      unpack8<T>(gw[i], g);
+      unpack8<T>(bw[i], bb);  // zeros without a beta
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * inv * g[j] + bb[j];
       *reinterpret_cast<uint4*>(y + row * ldy + (int64_t)c * 8) = pack8<T>(o);
