@@ -6,9 +6,15 @@
 // re-stages its operands, so the step runs at ~22% of HBM although its work
 // is one pass over the weights.  Here one CTA per SM stays resident for the
 // whole step:
-//  * consumer warps 0..14 run the phases; a grid-wide barrier (an atomic
-//    arrival count and a generation word in global memory, bounded waits)
-//    separates a phase from the next one that reads its output;
+//  * consumer warps 0..14 run the phases.  A phase's output (QKV rows,
+//    attention output, residual stream, SwiGLU output) goes to the
+//    workspace as 64-bit words {value, epoch of the writing phase}; the
+//    next phase polls the words it reads until all carry that epoch, so the
+//    data load is the synchronisation (no separate grid barrier).  Every
+//    phase reads the whole output of the previous one, so no CTA can run
+//    more than one phase ahead of another and a buffer is never rewritten
+//    while it is still read.  One grid-wide barrier (an atomic arrival count
+//    in global memory, bounded waits) per step precedes the final argmax;
 //  * producer warp 15 streams this CTA's weight slice of every phase, in
 //    phase order, through two 96 KB shared-memory slots with bulk copies
 //    (cp.async.bulk, mbarrier completion).  Weights do not depend on the
@@ -62,12 +68,16 @@ struct Ws {
   uint32_t* count;      // barrier arrivals
   uint32_t* gen;        // barrier generation
   uint32_t* abortf;     // set when any wait gave up: every CTA winds down
-  void* x;              // [E] residual stream (dtype)
-  void* qkv;            // [(Hq+2Hkv) D]
+  // Activations exchanged between CTAs are tagged words: the value (fp32 of
+  // the dtype-rounded number) in the low half, the epoch of the phase that
+  // wrote it in the high half; one 64-bit store / load is single-copy
+  // atomic, so a reader that sees the current epoch sees the value too.
+  uint64_t* x;          // [E] residual stream
+  uint64_t* qkv;        // [(Hq+2Hkv) D]
   float* part;          // [Hq][S][D + 2] attention partials (o, m, l)
-  void* o;              // [Hq D] merged attention output
+  uint64_t* o;          // [Hq D] merged attention output
   uint32_t* head_cnt;   // [Hkv] attention units finished (self-resetting)
-  void* ff;             // [F] SwiGLU output
+  uint64_t* ff;         // [F] SwiGLU output
   float* amax_v;        // [CTAs] per-CTA best logit
   int* amax_i;          // [CTAs] its index
 };
@@ -79,19 +89,20 @@ __host__ __device__ inline size_t ws_layout(char* base, int64_t E, int64_t Hq, i
   size_t off = 0;
   auto take = [&](size_t bytes) { char* p = base + off; off += al256(bytes); return p; };
   char* sync = take(256 + 4 * 64);
-  char* x = take((size_t)E * 2);
-  char* qkv = take((size_t)(Hq + 2 * Hkv) * D * 2);
+  char* x = take((size_t)E * 8);
+  char* qkv = take((size_t)(Hq + 2 * Hkv) * D * 8);
   char* part = take((size_t)Hq * kMaxCTAs * (D + 2) * 4);
-  char* o = take((size_t)Hq * D * 2);
-  char* ff = take((size_t)F * 2);
+  char* o = take((size_t)Hq * D * 8);
+  char* ff = take((size_t)F * 8);
   char* av = take((size_t)kMaxCTAs * 4);
   char* ai = take((size_t)kMaxCTAs * 4);
   if (w) {
     w->count = reinterpret_cast<uint32_t*>(sync);
     w->gen = reinterpret_cast<uint32_t*>(sync + 64);
     w->abortf = reinterpret_cast<uint32_t*>(sync + 128);
-    w->x = x; w->qkv = qkv; w->o = o;
-    w->head_cnt = reinterpret_cast<uint32_t*>(sync + 256); w->part = reinterpret_cast<float*>(part); w->ff = ff;
+    w->x = reinterpret_cast<uint64_t*>(x); w->qkv = reinterpret_cast<uint64_t*>(qkv);
+    w->o = reinterpret_cast<uint64_t*>(o);
+    w->head_cnt = reinterpret_cast<uint32_t*>(sync + 256); w->part = reinterpret_cast<float*>(part); w->ff = reinterpret_cast<uint64_t*>(ff);
     w->amax_v = reinterpret_cast<float*>(av); w->amax_i = reinterpret_cast<int*>(ai);
   }
   return off;
@@ -174,6 +185,42 @@ __device__ __forceinline__ bool grid_sync(const Ws& w, unsigned long long& targe
   return grid_wait(w, target, flag, err, code);
 }
 
+// ---- tagged activation words ----
+__device__ __forceinline__ void st_tag(uint64_t* p, float v, uint32_t ep) {
+  const uint64_t wv = ((uint64_t)ep << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(wv) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tag(const uint64_t* p) {
+  uint64_t wv;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(wv) : "l"(p) : "memory");
+  return wv;
+}
+// Polls n tagged words (n <= kPollMax, all loads of a round in flight at
+// once) until every one carries epoch ep; bounded, gives up when another
+// CTA aborted.  Returns false on give-up (error code set, abort raised).
+constexpr int kPollMax = 8;
+template <int N>
+__device__ __forceinline__ bool poll_tags(const uint64_t* const (&src)[N], int n, uint32_t ep,
+                                          uint64_t (&v)[N], const Ws& w, int* err, int code) {
+#pragma unroll
+  for (int u = 0; u < N; ++u) v[u] = u < n ? ld_tag(src[u]) : ((uint64_t)ep << 32);
+  for (uint32_t it = 0;; ++it) {
+    bool all = true;
+#pragma unroll
+    for (int u = 0; u < N; ++u) all = all && (uint32_t)(v[u] >> 32) == ep;
+    if (all) return true;
+    if (it >= kSpinLimit) {
+      if (err) atomicExch(err, code);
+      atomicExch(w.abortf, 1u);
+      return false;
+    }
+    if ((it & 255) == 255 && ld_acquire(w.abortf) != 0) return false;
+#pragma unroll
+    for (int u = 0; u < N; ++u)
+      if (u < n && (uint32_t)(v[u] >> 32) != ep) v[u] = ld_tag(src[u]);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float ldT(const void* p, int64_t i) {
   return to_f32(__ldcg(static_cast<const T*>(p) + i));
@@ -199,6 +246,39 @@ __device__ __forceinline__ void load_vec(uint16_t* xh, const void* src, int n, i
       for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
     }
     reinterpret_cast<uint4*>(xh)[i] = u;
+  }
+  if (red != nullptr) {
+    ss = warp_sum(ss);
+    if ((ctid & 31) == 0) red[ctid >> 5] = ss;
+  }
+}
+// xh[0..n) = the tagged vector src[0..n) once every word carries epoch ep
+// (the phase that writes it has finished in every CTA), as load_vec.  On
+// give-up sets *fail.
+template <typename T>
+__device__ __forceinline__ void load_tagged(uint16_t* xh, const uint64_t* src, int n,
+                                            uint32_t ep, int ctid, float* red, const Ws& w,
+                                            int* err, int code, int* fail) {
+  const uint64_t* ptr[kPollMax];
+  int m = 0;
+#pragma unroll
+  for (int u = 0; u < kPollMax; ++u) {
+    const int i = ctid + u * kCons;
+    ptr[u] = src + (i < n ? i : 0);
+    m += i < n ? 1 : 0;
+  }
+  uint64_t v[kPollMax];
+  if (!poll_tags<kPollMax>(ptr, m, ep, v, w, err, code)) *(volatile int*)fail = 1;
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < kPollMax; ++u) {
+    const int i = ctid + u * kCons;
+    if (i < n) {
+      const float f = __uint_as_float((uint32_t)v[u]);
+      ss = fmaf(f, f, ss);
+      const T t = from_f32<T>(f);
+      xh[i] = *reinterpret_cast<const uint16_t*>(&t);
+    }
   }
   if (red != nullptr) {
     ss = warp_sum(ss);
@@ -414,6 +494,8 @@ struct Smem {
   int kv_issued;              // layers whose K/V staging the producer issued
   int kvfail;                 // a staged-K/V wait gave up
   int flag;
+  int poll_fail;              // a tagged-vector poll gave up
+  uint32_t ep_base;           // this step's epoch base
   int abort_local;            // consumers gave up: the producer stops
   int issued;                 // jobs the producer issued
 };
@@ -557,7 +639,16 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       asm volatile("ld.acquire.gpu.global.u64 %0, [%1];"
                    : "=l"(v) : "l"(reinterpret_cast<unsigned long long*>(w.count)) : "memory");
       bar_target = v / gridDim.x * gridDim.x;
+      // one grid barrier per step: v / G steps have run; epochs of this
+      // step's phases follow those of every earlier step
+      sm.ep_base = (uint32_t)(v / gridDim.x) * (uint32_t)(5 * a.n_layers + 2);
+      sm.poll_fail = 0;
     }
+    cons_sync();
+    const uint32_t ep_base = sm.ep_base;
+    // epoch of phase ph (0 QKV, 1 attention, 2 o-proj, 3 gate/up, 4 down) of layer l
+    auto ep = [&](int l, int ph) { return ep_base + (uint32_t)(5 * l + ph + 1); };
+    auto polled = [&]() { return *(volatile int*)&sm.poll_fail == 0; };
     const int64_t tok = a.tokens[0];
     const int pos = a.positions[0];
     const int R = (a.Hq + 2 * a.Hkv) * a.D;
@@ -574,13 +665,16 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
     int r0, r1;
     for (int l = 0; l < a.n_layers && ok; ++l) {
       const tpp_decode_layer& L = a.layers[l];
-      const void* xsrc = l == 0 ? emb_row : w.x;
       // ---- QKV: qkv[r] = (x . Wqkv_f[r]) * rsqrt(mean(x^2) + eps) ----
       {
         const uint8_t* sl = acquire();
         DP_TS(8 + l * 16 + 0);
-        load_vec<T>(sm.xh, xsrc, a.E, ctid, sm.red);
+        if (l == 0)
+          load_vec<T>(sm.xh, emb_row, a.E, ctid, sm.red);
+        else
+          load_tagged<T>(sm.xh, w.x, a.E, ep(l - 1, 4), ctid, sm.red, w, a.err, 62, &sm.poll_fail);
         cons_sync();
+        if (!polled()) { release(); ok = false; break; }
         DP_TS(8 + l * 16 + 14);
         {  // this CTA's residual rows, for the o-proj and down phases
           const int e0 = sh.e0, e1 = sh.e1;
@@ -593,10 +687,9 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         DP_TS(8 + l * 16 + 1);
         release();
         for (int r = ctid; r < r1 - r0; r += kCons)
-          static_cast<T*>(w.qkv)[r0 + r] = from_f32<T>(row_sum(sm.gpart, r1 - r0, a.E, r) * rs);
+          st_tag(w.qkv + r0 + r, rndT<T>(row_sum(sm.gpart, r1 - r0, a.E, r) * rs), ep(l, 0));
       }
       if (!ok) break;
-      grid_arrive(w, bar_target);
       constexpr int NW = kCons / 32;
       const int S = au.S, h = au.h, sp = au.sp, k0 = au.k0, kend = au.kend, ktot = au.ktot;
       const int nst = au.nst;
@@ -605,7 +698,6 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
       const T* vc = static_cast<const T*>(L.vc) + (int64_t)h * a.Smax * 128;
       // staged rows: K [nst][128], V [nst][128], q-norm, k-norm weights
       const T* kvs = reinterpret_cast<const T*>(slot[(4 * l + 1) & 1] + o_bytes);
-      if (!grid_wait(w, bar_target, &sm.flag, a.err, 62)) { ok = false; break; }
       DP_TS(8 + l * 16 + 2);
       // ---- attention ----
       {
@@ -627,14 +719,18 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           }
           // q rows of the G query heads, the new k row (normed + rotated) and v row
           if (warp <= GQ + 1) {
-            const T* qkv = static_cast<const T*>(w.qkv);
             const int row = warp < GQ ? (h * GQ + warp) : (warp == GQ ? a.Hq + h : a.Hq + a.Hkv + h);
             float x[4];
             {
-              const uint2 u = __ldcg(reinterpret_cast<const uint2*>(qkv + (int64_t)row * D + lane * 4));
-              const T* e = reinterpret_cast<const T*>(&u);
+              // the row's four tagged words of this lane, once QKV of this
+              // layer has stored them
+              const uint64_t* src = w.qkv + (int64_t)row * D + lane * 4;
+              const uint64_t* const ptr[4] = {src, src + 1, src + 2, src + 3};
+              uint64_t v4[4];
+              if (!poll_tags<4>(ptr, 4, ep(l, 0), v4, w, a.err, 70)) sm.kvfail = 1;
 #pragma unroll
-              for (int j = 0; j < 4; ++j) x[j] = to_f32(e[j]);
+              for (int j = 0; j < 4; ++j) x[j] = __uint_as_float((uint32_t)v4[j]);
+              __syncwarp();
             }
             if (l < 2) DP_TS(476 + l * 10);
             if (warp <= GQ) {
@@ -867,8 +963,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
                   }
                   M = mc;
                 }
-                static_cast<T*>(w.o)[(int64_t)(h * GQ + g) * 128 + d] =
-                    from_f32<T>(den > 0.f ? num / den : 0.f);
+                st_tag(w.o + (int64_t)(h * GQ + g) * 128 + d, rndT<T>(den > 0.f ? num / den : 0.f),
+                       ep(l, 1));
               }
             }
           }
@@ -876,33 +972,35 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         }
       }
       DP_TS(8 + l * 16 + 3);
-      if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 63)) { ok = false; break; }
+      if (!ok) break;
       DP_TS(8 + l * 16 + 4);
       // ---- o-proj + residual: x[r] = x[r] + o . Wo[r] ----
       {
         const uint8_t* sl = acquire();
         DP_TS(8 + l * 16 + 5);
         const int K = a.Hq * a.D;
-        load_vec<T>(sm.xh, w.o, K, ctid);
+        load_tagged<T>(sm.xh, w.o, K, ep(l, 1), ctid, nullptr, w, a.err, 63, &sm.poll_fail);
         cons_sync();
+        if (!polled()) { release(); ok = false; break; }
         DP_TS(8 + l * 16 + 15);
         r0 = sh.e0; r1 = sh.e1;
         slice_dot<T>(smem_u32(sl), r1 - r0, K, xs_s, sm.gpart, warp, lane);
         release();
         for (int r = ctid; r < r1 - r0; r += kCons) {
           const T nv = from_f32<T>(sm.xres[r] + row_sum(sm.gpart, r1 - r0, K, r));
-          static_cast<T*>(w.x)[r0 + r] = nv;
+          st_tag(w.x + r0 + r, to_f32(nv), ep(l, 2));
           sm.xres[r] = to_f32(nv);
         }
       }
       DP_TS(8 + l * 16 + 6);
-      if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 64)) { ok = false; break; }
+      if (!ok) break;
       DP_TS(8 + l * 16 + 7);
       // ---- gate/up + SwiGLU: ff[f] = silu(g * rs) * (u * rs) ----
       {
         const uint8_t* sl = acquire();
-        load_vec<T>(sm.xh, w.x, a.E, ctid, sm.red);
+        load_tagged<T>(sm.xh, w.x, a.E, ep(l, 2), ctid, sm.red, w, a.err, 64, &sm.poll_fail);
         cons_sync();
+        if (!polled()) { release(); ok = false; break; }
         DP_TS(8 + l * 16 + 8);
         r0 = sh.f0; r1 = sh.f1;
         const int nf = r1 - r0;
@@ -913,35 +1011,40 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
         for (int f = ctid; f < nf; f += kCons) {
           const float g = row_sum(sm.gpart, 2 * nf, a.E, f);
           const float u = row_sum(sm.gpart, 2 * nf, a.E, nf + f);
-          static_cast<T*>(w.ff)[r0 + f] = from_f32<T>(act_silu(g * rs) * (u * rs));
+          st_tag(w.ff + r0 + f, rndT<T>(act_silu(g * rs) * (u * rs)), ep(l, 3));
         }
       }
       DP_TS(8 + l * 16 + 9);
-      if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 65)) { ok = false; break; }
+      if (!ok) break;
       DP_TS(8 + l * 16 + 10);
       // ---- down + residual: x[r] = x[r] + ff . Wd[r] ----
       {
         const uint8_t* sl = acquire();
-        load_vec<T>(sm.xh, w.ff, a.F, ctid);
+        load_tagged<T>(sm.xh, w.ff, a.F, ep(l, 3), ctid, nullptr, w, a.err, 65, &sm.poll_fail);
         cons_sync();
+        if (!polled()) { release(); ok = false; break; }
         DP_TS(8 + l * 16 + 11);
         r0 = sh.e0; r1 = sh.e1;
         slice_dot<T>(smem_u32(sl), r1 - r0, a.F, xs_s, sm.gpart, warp, lane);
         release();
         for (int r = ctid; r < r1 - r0; r += kCons) {
           const T nv = from_f32<T>(sm.xres[r] + row_sum(sm.gpart, r1 - r0, a.F, r));
-          static_cast<T*>(w.x)[r0 + r] = nv;
+          st_tag(w.x + r0 + r, to_f32(nv), ep(l, 4));
           sm.xres[r] = to_f32(nv);
         }
       }
       DP_TS(8 + l * 16 + 12);
-      if (!ok || !grid_sync(w, bar_target, &sm.flag, a.err, 66)) { ok = false; break; }
+      if (!ok) break;
       DP_TS(8 + l * 16 + 13);
     }
     // ---- LM head: logits = (x . Wh_f) * rs, per-CTA argmax ----
     if (ok) {
-      load_vec<T>(sm.xh, w.x, a.E, ctid, sm.red);
+      load_tagged<T>(sm.xh, w.x, a.E, ep(a.n_layers - 1, 4), ctid, sm.red, w, a.err, 66,
+                     &sm.poll_fail);
       cons_sync();
+      ok = polled();
+    }
+    if (ok) {
       const float rs = rsqrtf(sumsq_of(sm.red) * inv_e + a.eps);
       const int v0 = sh.v0, v1 = sh.v1;
       float bv = -INFINITY;
