@@ -436,7 +436,7 @@ int64_t tpp_decode_step_persistent_workspace(int64_t E, int64_t Hq, int64_t Hkv,
  * raises the device error flag and the kernel returns) instead of kernel
  * boundaries,
  * and each CTA's producer warp streams the weight slices of the coming
- * phases (paced: TPP_DP_PACE="<KiB>,<in flight>", default "8,6") and its
+ * phases (paced: TPP_DP_PACE="<KiB>,<in flight>", default "16,8") and its
  * attention unit's cached K/V rows into shared memory across the barriers.  cos/sin: fp16 RoPE tables
  * [ctx, D] (row stride cs_stride); dtype bf16 or fp16.  Replaces the
  * reference's per-token loop of torchpp/llmops/llm.py:263-282 over

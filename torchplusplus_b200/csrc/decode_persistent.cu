@@ -1191,8 +1191,8 @@ extern "C" int tpp_decode_step_persistent(
   a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
   a.lm_rows_per_job = (int)(kSlot / ((E + kPad) * 2));
   // TPP_DP_PACE="<chunk KiB>,<chunks in flight>" (",0": one burst per slice)
-  a.pace_chunk = 8 * 1024;
-  a.pace_depth = 6;
+  a.pace_chunk = 16 * 1024;
+  a.pace_depth = 8;
   if (const char* pe = getenv("TPP_DP_PACE")) {
     int kb = 0, d = 0;
     if (sscanf(pe, "%d,%d", &kb, &d) == 2 && kb >= 1 && kb <= 96 && d >= 0 && d <= kPaceMax) {
