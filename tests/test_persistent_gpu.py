@@ -102,3 +102,20 @@ def test_persistent_step_at_qwen3_widths(prompt):
             la, lb = ea.logits.float(), eb.logits.float()
             assert (la - lb).abs().max().item() <= 2e-2 * max(1.0, lb.abs().max().item()), step
     assert ops.device_error() == 0
+
+
+def test_persistent_steps_repeat_exactly_across_requests():
+    """The step kernel tags every exchanged activation with an epoch derived
+    from the steps already run on its workspace; a second request on the
+    same engine (epochs continuing, graph replays) must pick the same tokens
+    as the first."""
+    m = _model(torch.bfloat16, seed=4)
+    ids = torch.randint(0, 1000, (1, 45), generator=torch.Generator().manual_seed(11))
+    m.decode_persistent = True
+    with torch.inference_mode():
+        a = m.generate(ids, max_new_token=24, sampling_strategy="greedy").cpu()
+        eng = m._engine
+        b = m.generate(ids, max_new_token=24, sampling_strategy="greedy").cpu()
+        assert m._engine is eng and eng.persistent is not None
+    assert torch.equal(a, b)
+    assert ops.device_error() == 0
