@@ -23,7 +23,7 @@
 //  * per layer: QKV (RMSNorm folded into the weights, each CTA a contiguous
 //    row range) | attention (kv head x key-range units; q/k RMSNorm + RoPE
 //    and the K/V append of the new token in the unit that owns its
-//    position; the last unit of a head to finish merges the head's
+//    position; unit 0 of a head merges the head's
 //    partials) | o-proj + residual | gate/up + SwiGLU | down + residual;
 //    then the LM head (row chunks, per-CTA argmax) and the token bookkeeping.
 // GEMVs run on CUDA cores (one token: one weight byte is used once), a warp
@@ -74,9 +74,8 @@ struct Ws {
   // atomic, so a reader that sees the current epoch sees the value too.
   uint64_t* x;          // [E] residual stream
   uint64_t* qkv;        // [(Hq+2Hkv) D]
-  float* part;          // [Hq][S][D + 2] attention partials (o, m, l)
+  uint64_t* part;       // [Hq][S][D + 2] attention partials (o, m, l), tagged
   uint64_t* o;          // [Hq D] merged attention output
-  uint32_t* head_cnt;   // [Hkv] attention units finished (self-resetting)
   uint64_t* ff;         // [F] SwiGLU output
   float* amax_v;        // [CTAs] per-CTA best logit
   int* amax_i;          // [CTAs] its index
@@ -91,7 +90,7 @@ __host__ __device__ inline size_t ws_layout(char* base, int64_t E, int64_t Hq, i
   char* sync = take(256 + 4 * 64);
   char* x = take((size_t)E * 8);
   char* qkv = take((size_t)(Hq + 2 * Hkv) * D * 8);
-  char* part = take((size_t)Hq * kMaxCTAs * (D + 2) * 4);
+  char* part = take((size_t)Hq * kMaxCTAs * (D + 2) * 8);
   char* o = take((size_t)Hq * D * 8);
   char* ff = take((size_t)F * 8);
   char* av = take((size_t)kMaxCTAs * 4);
@@ -102,7 +101,7 @@ __host__ __device__ inline size_t ws_layout(char* base, int64_t E, int64_t Hq, i
     w->abortf = reinterpret_cast<uint32_t*>(sync + 128);
     w->x = reinterpret_cast<uint64_t*>(x); w->qkv = reinterpret_cast<uint64_t*>(qkv);
     w->o = reinterpret_cast<uint64_t*>(o);
-    w->head_cnt = reinterpret_cast<uint32_t*>(sync + 256); w->part = reinterpret_cast<float*>(part); w->ff = reinterpret_cast<uint64_t*>(ff);
+    w->part = reinterpret_cast<uint64_t*>(part); w->ff = reinterpret_cast<uint64_t*>(ff);
     w->amax_v = reinterpret_cast<float*>(av); w->amax_i = reinterpret_cast<int*>(ai);
   }
   return off;
@@ -911,53 +910,57 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
               } else {
                 t = sm.oacc[g][d];
               }
-              float* dst = w.part + ((int64_t)(h * GQ + g) * S + sp) * (128 + 2);
-              dst[d] = t;
-              if (d == 0) { dst[128] = sm.mrun[g]; dst[129] = sm.lrun[g]; }
+              uint64_t* dst = w.part + ((int64_t)(h * GQ + g) * S + sp) * (128 + 2);
+              st_tag(dst + d, t, ep(l, 1));
+              if (d == 0) {
+                st_tag(dst + 128, sm.mrun[g], ep(l, 1));
+                st_tag(dst + 129, sm.lrun[g], ep(l, 1));
+              }
             }
-            cons_sync();
             if (l < 2) DP_TS(474 + l * 10);
-            // the last unit of head h to finish merges its S partials.  The
-            // counter add is acq_rel at gpu scope: it releases this unit's
-            // partial (ordered before it by the CTA barrier) and, in the last
-            // unit, acquires every other unit's.
-            if (ctid == 0) {
-              uint32_t prev;
-              asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                           : "=r"(prev) : "l"(w.head_cnt + h) : "memory");
-              const bool last = prev == (uint32_t)(S - 1);
-              if (last) atomicExch(&w.head_cnt[h], 0u);
-              sm.flag = last ? 1 : 0;
-            }
-            cons_sync();
-            if (sm.flag) {
-              // one (query head, dim) pair per thread; the S partials' (o, m,
-              // l) are loaded 8 at a time with every load of a group in flight
-              // and folded with a running max
+            // unit 0 of head h merges the S partials once every one carries
+            // this layer's epoch (no hand-shake between the units: the poll
+            // of the tagged partials is the wait).  One (query head, dim)
+            // pair per thread; the partials' (o, m, l) 8 at a time, every
+            // load of a group in flight, folded with a running max.
+            if (sp == 0) {
               for (int pi = ctid; pi < npair; pi += kCons) {
                 const int g = pi / 128, d = pi % 128;
-                const float* src = w.part + (int64_t)(h * GQ + g) * S * 130;
+                const uint64_t* src = w.part + (int64_t)(h * GQ + g) * S * 130;
                 float M = -INFINITY, den = 0.f, num = 0.f;
                 for (int s0 = 0; s0 < S; s0 += 8) {
+                  const int nin = min(8, S - s0);
+                  const uint64_t* ptr[24];
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) {
+                    const uint64_t* sp2 = src + (int64_t)(s0 + (u < nin ? u : 0)) * 130;
+                    ptr[u] = sp2 + 128;
+                    ptr[8 + u] = sp2 + 129;
+                    ptr[16 + u] = sp2 + d;
+                  }
+                  uint64_t tv[24];
+                  if (!poll_tags<24>(ptr, 24, ep(l, 1), tv, w, a.err, 71)) {
+                    *(volatile int*)&sm.poll_fail = 1;
+                    break;
+                  }
                   float mv[8], lv[8], ov[8];
 #pragma unroll
                   for (int u = 0; u < 8; ++u) {
-                    const bool in = s0 + u < S;
-                    const float* sp2 = src + (int64_t)(s0 + u) * 130;
-                    mv[u] = in ? __ldcg(sp2 + 128) : -INFINITY;
-                    lv[u] = in ? __ldcg(sp2 + 129) : 0.f;
-                    ov[u] = in ? __ldcg(sp2 + d) : 0.f;
+                    const bool in = u < nin;
+                    mv[u] = in ? __uint_as_float((uint32_t)tv[u]) : -INFINITY;
+                    lv[u] = in ? __uint_as_float((uint32_t)tv[8 + u]) : 0.f;
+                    ov[u] = in ? __uint_as_float((uint32_t)tv[16 + u]) : 0.f;
                   }
                   float mc = M;
 #pragma unroll
                   for (int u = 0; u < 8; ++u) mc = fmaxf(mc, mv[u]);
                   if (mc == -INFINITY) continue;
-                  const float cr = M == -INFINITY ? 0.f : exp2f(M - mc);
+                  const float cr = M == -INFINITY ? 0.f : ex2_ftz(M - mc);
                   den *= cr;
                   num *= cr;
 #pragma unroll
                   for (int u = 0; u < 8; ++u) {
-                    const float e = mv[u] == -INFINITY ? 0.f : exp2f(mv[u] - mc);
+                    const float e = mv[u] == -INFINITY ? 0.f : ex2_ftz(mv[u] - mc);
                     den = fmaf(e, lv[u], den);
                     num = fmaf(e, ov[u], num);
                   }
@@ -966,6 +969,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
                 st_tag(w.o + (int64_t)(h * GQ + g) * 128 + d, rndT<T>(den > 0.f ? num / den : 0.f),
                        ep(l, 1));
               }
+              cons_sync();
+              if (!polled()) ok = false;
             }
           }
           if (l < 2) DP_TS(475 + l * 10);
