@@ -431,10 +431,10 @@ int64_t tpp_decode_step_persistent_workspace(int64_t E, int64_t Hq, int64_t Hkv,
  * written, [V] in dtype; pitch E + TPP_PERSISTENT_ROW_PAD) -> argmax -> tokens[0] = next, out_ids[p+1] = next
  * (if p+1 < out_cap), positions[0] = p+1, seqlens[0] = p+2.  The phases
  * exchange their outputs as epoch-tagged words in the workspace, so a phase
- * starts once the words it reads carry its producer phase's epoch, with one
- * grid-wide barrier per step before the argmax (bounded waits; an expiry
- * raises the device error flag and the kernel returns) instead of kernel
- * boundaries,
+ * starts once the words it reads carry its producer phase's epoch, and CTA
+ * 0 picks the token once every CTA's tagged best logit has arrived (bounded
+ * waits; an expiry raises the device error flag and the kernel returns)
+ * instead of kernel boundaries,
  * and each CTA's producer warp streams the weight slices of the coming
  * phases (paced: TPP_DP_PACE="<KiB>,<in flight>", default "16,8") and its
  * attention unit's cached K/V rows into shared memory across the barriers.  cos/sin: fp16 RoPE tables

@@ -13,8 +13,10 @@
 //    data load is the synchronisation (no separate grid barrier).  Every
 //    phase reads the whole output of the previous one, so no CTA can run
 //    more than one phase ahead of another and a buffer is never rewritten
-//    while it is still read.  One grid-wide barrier (an atomic arrival count
-//    in global memory, bounded waits) per step precedes the final argmax;
+//    while it is still read.  The per-CTA argmax picks are tagged words
+//    too; CTA 0 polls them and writes the token, the others count
+//    themselves in (an atomic arrival count that numbers the steps, and so
+//    the epochs) and leave;
 //  * producer warp 15 streams this CTA's weight slice of every phase, in
 //    phase order, through two 96 KB shared-memory slots with bulk copies
 //    (cp.async.bulk, mbarrier completion).  Weights do not depend on the
@@ -77,8 +79,8 @@ struct Ws {
   uint64_t* part;       // [Hq][S][D + 2] attention partials (o, m, l), tagged
   uint64_t* o;          // [Hq D] merged attention output
   uint64_t* ff;         // [F] SwiGLU output
-  float* amax_v;        // [CTAs] per-CTA best logit
-  int* amax_i;          // [CTAs] its index
+  uint64_t* amax_v;     // [CTAs] per-CTA best logit (tagged)
+  uint64_t* amax_i;     // [CTAs] its index (tagged, bits of the int)
 };
 
 __host__ __device__ inline size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
@@ -93,8 +95,8 @@ __host__ __device__ inline size_t ws_layout(char* base, int64_t E, int64_t Hq, i
   char* part = take((size_t)Hq * kMaxCTAs * (D + 2) * 8);
   char* o = take((size_t)Hq * D * 8);
   char* ff = take((size_t)F * 8);
-  char* av = take((size_t)kMaxCTAs * 4);
-  char* ai = take((size_t)kMaxCTAs * 4);
+  char* av = take((size_t)kMaxCTAs * 8);
+  char* ai = take((size_t)kMaxCTAs * 8);
   if (w) {
     w->count = reinterpret_cast<uint32_t*>(sync);
     w->gen = reinterpret_cast<uint32_t*>(sync + 64);
@@ -102,7 +104,7 @@ __host__ __device__ inline size_t ws_layout(char* base, int64_t E, int64_t Hq, i
     w->x = reinterpret_cast<uint64_t*>(x); w->qkv = reinterpret_cast<uint64_t*>(qkv);
     w->o = reinterpret_cast<uint64_t*>(o);
     w->part = reinterpret_cast<uint64_t*>(part); w->ff = reinterpret_cast<uint64_t*>(ff);
-    w->amax_v = reinterpret_cast<float*>(av); w->amax_i = reinterpret_cast<int*>(ai);
+    w->amax_v = reinterpret_cast<uint64_t*>(av); w->amax_i = reinterpret_cast<uint64_t*>(ai);
   }
   return off;
 }
@@ -1082,18 +1084,34 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
             bv = sm.best_v[i];
             bi = sm.best_i[i];
           }
-        w.amax_v[c] = bv;
-        w.amax_i[c] = bi;
+        st_tag(w.amax_v + c, bv, ep(a.n_layers, 0));
+        st_tag(w.amax_i + c, __int_as_float(bi), ep(a.n_layers, 0));
       }
       DP_TS(500);
-      ok = grid_sync(w, bar_target, &sm.flag, a.err, 67);
+      // every CTA counts itself in for this step (the count sets the next
+      // step's epochs) and leaves; CTA 0 waits for the others' tagged picks
+      grid_arrive(w, bar_target);
       DP_TS(501);
       if (ok && c == 0 && warp == 0) {
         float v = -INFINITY;
         int idx = 0x7fffffff;
-        for (int i = lane; i < G; i += 32) {
-          const float vv = __ldcg(w.amax_v + i);
-          const int ii = __ldcg(w.amax_i + i);
+        const uint64_t* ptr[16];
+        int n = 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = lane + 32 * u;
+          const int ic = i < G ? i : 0;
+          ptr[u] = w.amax_v + ic;
+          ptr[8 + u] = w.amax_i + ic;
+        }
+        for (int u = 0; u < 8; ++u) n += lane + 32 * u < G ? 1 : 0;
+        uint64_t tv[16];
+        if (!poll_tags<16>(ptr, 16, ep(a.n_layers, 0), tv, w, a.err, 67)) ok = false;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u >= n) break;
+          const float vv = __uint_as_float((uint32_t)tv[u]);
+          const int ii = (int)(uint32_t)tv[8 + u];
           if (vv > v || (vv == v && ii < idx)) { v = vv; idx = ii; }
         }
 #pragma unroll
@@ -1102,7 +1120,8 @@ __global__ void __launch_bounds__(kThr, 1) decode_step_kernel(const StepArgs a) 
           const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
           if (v2 > v || (v2 == v && i2 < idx)) { v = v2; idx = i2; }
         }
-        if (lane == 0) {
+        const bool all_ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0 && all_ok) {
           const int p1 = pos + 1;
           a.tokens[0] = idx;
           if (a.out_ids != nullptr && p1 < a.out_cap) a.out_ids[p1] = idx;
