@@ -138,7 +138,7 @@ class DecodeEngine:
         # batch 1, native weights: the whole step as one persistent
         # cooperative kernel (tpp_decode_step_persistent) unless turned off
         # (persistent=False or TPP_PERSISTENT=0).  Qwen3-0.6B shape, context
-        # ~640: 743 us a step against 864 us for the launch-per-phase graph.
+        # ~640: ~580 us a step against ~865 us for the launch-per-phase graph.
         self.persistent = None
         if persistent is None:
             persistent = os.environ.get("TPP_PERSISTENT", "1") != "0"
